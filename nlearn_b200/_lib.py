@@ -1,0 +1,86 @@
+"""ctypes binding of ``libnl_ops.so`` — the C ABI declared in ``include/nl_ops.h``.
+
+This is the same binding a ctypes- or FFI-based caller of the reference would
+add for its custom-call targets: plain pointers, sizes and a stream handle.
+Tensors are passed as ``tensor.data_ptr()``; the stream is the current torch
+CUDA stream, so kernels order with surrounding torch work and are captured by
+CUDA graphs.
+
+There is no fallback: if the library is missing, importing an operator that
+needs it raises, naming the build command.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_float, c_int, c_longlong, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libnl_ops.so")
+
+STATUS = {0: "NL_OK", -1: "NL_ERR_SHAPE", -2: "NL_ERR_ALIGN", -3: "NL_ERR_LAUNCH", -4: "NL_ERR_CUDA",
+          -5: "NL_ERR_DTYPE", -6: "NL_ERR_WORKSPACE"}
+F32, BF16 = 0, 1
+EPI_STORE, EPI_ACCUM, EPI_BIAS, EPI_BIAS_GELU, EPI_RESID = 0, 1, 2, 3, 4
+
+# name -> argtypes (restype is int unless listed in _RESTYPE)
+SIGNATURES: dict[str, list] = {
+    "nl_version": [],
+    "nl_get_device_error": [c_void_p],
+    "nl_gemm": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
+    "nl_gemm_ex": [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                   c_float, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
+}
+_RESTYPE = {"nl_version": ctypes.c_char_p}
+
+
+class NlError(RuntimeError):
+    """A kernel entry point returned a non-zero nl_status."""
+
+
+class _Lib:
+    def __init__(self) -> None:
+        self._dll = None
+
+    def _load(self):
+        if self._dll is None:
+            if not LIB_PATH.exists():
+                raise ImportError(f"{LIB_PATH} is missing: build it with `python -m nlearn_b200.build` "
+                                  "(there is no CPU fallback for the hot path)")
+            dll = ctypes.CDLL(str(LIB_PATH))
+            for name, args in SIGNATURES.items():
+                fn = getattr(dll, name)
+                fn.argtypes = args
+                fn.restype = _RESTYPE.get(name, c_int)
+            self._dll = dll
+        return self._dll
+
+    def __getattr__(self, name):
+        if name.startswith("nl_"):
+            return getattr(self._load(), name)
+        raise AttributeError(name)
+
+
+lib = _Lib()
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        raise NlError(f"{what} returned {STATUS.get(status, status)}")
+
+
+def stream_handle():
+    import torch
+    return c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def ptr(t) -> c_void_p:
+    return c_void_p(0 if t is None else t.data_ptr())
+
+
+def device_error() -> int:
+    """Read and clear the kernels' device error word (1 = a bounded wait gave up)."""
+    return lib.nl_get_device_error(stream_handle())
+
+
+__all__ = ["lib", "check", "ptr", "stream_handle", "device_error", "NlError", "LIB_PATH", "SIGNATURES",
+           "F32", "BF16", "EPI_STORE", "EPI_ACCUM", "EPI_BIAS", "EPI_BIAS_GELU", "EPI_RESID", "c_longlong"]

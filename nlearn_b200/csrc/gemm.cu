@@ -1,0 +1,436 @@
+// gemm.cu — persistent warp-specialised bf16 GEMM for sm_100a (tcgen05 + TMEM + TMA).
+//
+// Replaces nlearn's Metal `gemm_sg` (iree_metal/kernels/gemm.metal:48-115, C f32 =
+// A bf16 . B bf16 with 32x32 simdgroup tiles) and the transposes its backward
+// materialises (nlearn/kernels/gemm.py:71-76): either operand may be K-major or
+// MN-major in global memory, so dX = dY.W^T and dW = X^T.dY read the forward
+// tensors in place.
+//
+// CTA = 6 warps, one CTA per SM, persistent over output tiles:
+//   warp 0      TMA producer: A/B k-blocks (64 deep) into a STAGES-deep ring
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2..5  epilogue: tcgen05.ld of the f32 accumulator (one TMEM lane =
+//               one output row per thread), fused bias / GELU / residual /
+//               accumulate, vectorised stores
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
+// of tile i overlaps the main loop of tile i+1.  Split-K (for the long-K,
+// few-tile dW GEMMs) accumulates with vector float atomics.
+#include "sm100.cuh"
+#include "host_common.h"
+
+namespace nl {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // one 128-byte swizzle row of bf16
+constexpr int kThreads = 6 * 32;
+constexpr int kEpiWarp0 = 2;
+
+struct Params {
+  int M, N, K;
+  int tiles_m, tiles_n, split_k, kb_per_split, num_kb;
+  void* C;
+  long long ldc;
+  int c_bf16;
+  int epi;
+  float alpha;
+  const float* bias;
+  __nv_bfloat16* aux;
+  const void* resid;
+  int* err;
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+  static constexpr int B_BYTES = BN * BK * 2;  // 16 / 32 KB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ float gelu_tanh(float a) {
+  float u = 0.7978845608028654f * (a + 0.044715f * a * a * a);
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return 0.5f * a * (1.f + t);
+}
+
+// Decode a work unit into (m block, n block, split index) with an M-grouped
+// raster so that consecutive CTAs share B panels in L2.
+__device__ __forceinline__ void decode_unit(const Params& p, int u, int& mb, int& nb, int& sk) {
+  const int tiles = p.tiles_m * p.tiles_n;
+  sk = u / tiles;
+  int t = u - sk * tiles;
+  constexpr int G = 16;
+  const int per_group = G * p.tiles_n;
+  const int g = t / per_group;
+  const int first_m = g * G;
+  const int gsz = min(p.tiles_m - first_m, G);
+  const int r = t - g * per_group;
+  mb = first_m + r % gsz;
+  nb = r / gsz;
+}
+
+// Epilogue for one thread: row `row`, 32 consecutive columns from `col0`.
+__device__ __forceinline__ void epi_chunk(const Params& p, int row, int col0, float (&v)[32]) {
+  if (row >= p.M) return;
+  const bool full = (col0 + 32 <= p.N);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] *= p.alpha;
+  const int epi = p.epi;
+  if (p.bias && (epi == NL_EPI_BIAS || epi == NL_EPI_BIAS_GELU || epi == NL_EPI_RESID)) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] += (col0 + i < p.N) ? __ldg(p.bias + col0 + i) : 0.f;
+  }
+  const long long off = (long long)row * p.ldc + col0;
+  if (epi == NL_EPI_BIAS_GELU) {
+    __nv_bfloat16* cb = reinterpret_cast<__nv_bfloat16*>(p.C) + off;
+    __nv_bfloat16* ab = p.aux + off;
+    const bool vec = full && ((p.ldc & 7) == 0);
+    if (vec) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 a, c;
+        a.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+        a.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+        a.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+        a.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+        c.x = pack_bf16x2(gelu_tanh(v[8 * j + 0]), gelu_tanh(v[8 * j + 1]));
+        c.y = pack_bf16x2(gelu_tanh(v[8 * j + 2]), gelu_tanh(v[8 * j + 3]));
+        c.z = pack_bf16x2(gelu_tanh(v[8 * j + 4]), gelu_tanh(v[8 * j + 5]));
+        c.w = pack_bf16x2(gelu_tanh(v[8 * j + 6]), gelu_tanh(v[8 * j + 7]));
+        reinterpret_cast<uint4*>(ab)[j] = a;
+        reinterpret_cast<uint4*>(cb)[j] = c;
+      }
+    } else {
+      for (int i = 0; i < 32 && col0 + i < p.N; ++i) {
+        ab[i] = __float2bfloat16_rn(v[i]);
+        cb[i] = __float2bfloat16_rn(gelu_tanh(v[i]));
+      }
+    }
+    return;
+  }
+  if (epi == NL_EPI_RESID && p.resid) {
+    if (p.c_bf16) {
+      const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(p.resid) + off;
+      for (int i = 0; i < 32; ++i) v[i] += (col0 + i < p.N) ? __bfloat162float(rb[i]) : 0.f;
+    } else {
+      const float* rf = reinterpret_cast<const float*>(p.resid) + off;
+      for (int i = 0; i < 32; ++i) v[i] += (col0 + i < p.N) ? rf[i] : 0.f;
+    }
+  }
+  if (epi == NL_EPI_ACCUM) {
+    float* cf = reinterpret_cast<float*>(p.C) + off;
+    const bool vec = full && ((p.ldc & 3) == 0);
+    if (p.split_k > 1) {
+      if (vec) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          atomicAdd(reinterpret_cast<float4*>(cf) + j, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+      } else {
+        for (int i = 0; i < 32 && col0 + i < p.N; ++i) atomicAdd(cf + i, v[i]);
+      }
+    } else {
+      if (vec) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float4 o = reinterpret_cast<float4*>(cf)[j];
+          o.x += v[4 * j];
+          o.y += v[4 * j + 1];
+          o.z += v[4 * j + 2];
+          o.w += v[4 * j + 3];
+          reinterpret_cast<float4*>(cf)[j] = o;
+        }
+      } else {
+        for (int i = 0; i < 32 && col0 + i < p.N; ++i) cf[i] += v[i];
+      }
+    }
+    return;
+  }
+  // plain store (STORE / BIAS / RESID)
+  if (p.c_bf16) {
+    __nv_bfloat16* cb = reinterpret_cast<__nv_bfloat16*>(p.C) + off;
+    if (full && ((p.ldc & 7) == 0)) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 c;
+        c.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+        c.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+        c.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+        c.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+        reinterpret_cast<uint4*>(cb)[j] = c;
+      }
+    } else {
+      for (int i = 0; i < 32 && col0 + i < p.N; ++i) cb[i] = __float2bfloat16_rn(v[i]);
+    }
+  } else {
+    float* cf = reinterpret_cast<float*>(p.C) + off;
+    if (full && ((p.ldc & 3) == 0)) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        reinterpret_cast<float4*>(cf)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else {
+      for (int i = 0; i < 32 && col0 + i < p.N; ++i) cf[i] = v[i];
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* full_bar = bars;                       // [STAGES]
+  uint64_t* empty_bar = bars + C::STAGES;          // [STAGES]
+  uint64_t* tfull_bar = bars + 2 * C::STAGES;      // [2]
+  uint64_t* tempty_bar = bars + 2 * C::STAGES + 2; // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int num_units = p.tiles_m * p.tiles_n * p.split_k;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::STAGES; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull_bar[i], 1);
+      mbar_init(&tempty_bar[i], 4 * 32);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  Abort ab{abort_flag, p.err};
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        int mb, nb, sk;
+        decode_unit(p, u, mb, nb, sk);
+        const int kb0 = sk * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[s], ph ^ 1, ab)) { ok = false; break; }
+          uint8_t* sA = tiles + s * C::STAGE_BYTES;
+          uint8_t* sB = sA + C::A_BYTES;
+          mbar_expect_tx(&full_bar[s], C::STAGE_BYTES);
+          if (!A_MN) {
+            tma_load_2d(&tmA, &full_bar[s], sA, kb * BK, mb * BM);
+          } else {
+#pragma unroll
+            for (int h = 0; h < BM / 64; ++h) tma_load_2d(&tmA, &full_bar[s], sA + h * 8192, mb * BM + h * 64, kb * BK);
+          }
+          if (!B_MN) {
+            tma_load_2d(&tmB, &full_bar[s], sB, kb * BK, nb * BN);
+          } else {
+#pragma unroll
+            for (int h = 0; h < BN / 64; ++h) tma_load_2d(&tmB, &full_bar[s], sB + h * 8192, nb * BN + h * 64, kb * BK);
+          }
+          if (++s == C::STAGES) { s = 0; ph ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+      int s = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t acc_ph = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        int mb, nb, sk;
+        decode_unit(p, u, mb, nb, sk);
+        const int kb0 = sk * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1, ab)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full_bar[s], ph, ab)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(tiles + s * C::STAGE_BYTES);
+          const uint32_t b0 = a0 + C::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sdesc_sw128(a0 + k * 2048, 8192, 1024) : sdesc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b0 + k * 2048, 8192, 1024) : sdesc_sw128(b0 + k * 32, 16, 1024);
+            umma_f16_ss(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[s]);
+          if (++s == C::STAGES) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+      int mb, nb, sk;
+      decode_unit(p, u, mb, nb, sk);
+      if (!mbar_wait(&tfull_bar[acc], acc_ph, ab)) break;
+      tc_fence_after();
+      const int row = mb * BM + q * 32 + lane;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col0 = nb * BN + c * 32;
+        if (col0 >= p.N) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld32(taddr + c * 32, r);
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        epi_chunk(p, row, col0, v);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_ph ^= 1;
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+template <int BN, bool A_MN, bool B_MN>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, Params& p, cudaStream_t stream) {
+  using C = Cfg<BN>;
+  auto kern = gemm_kernel<BN, A_MN, B_MN>;
+  static int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+      return NL_ERR_LAUNCH;
+    configured_dev = dev;
+  }
+  const int units = p.tiles_m * p.tiles_n * p.split_k;
+  const int grid = units < sm_count() ? units : sm_count();
+  kern<<<grid, kThreads, C::SMEM, stream>>>(ta, tb, p);
+  return launch_status();
+}
+
+}  // namespace gemm
+
+// Device error word shared by all kernels of this library (per device).
+int* device_error_word();
+
+int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long ldb, int b_trans, void* Cp,
+             long long ldc, int c_dtype, int M, int N, int K, float alpha, int epi, const float* bias, void* aux,
+             const void* resid, cudaStream_t stream) {
+  using namespace gemm;
+  if (M <= 0 || N <= 0 || K < 0) return NL_ERR_SHAPE;
+  if (c_dtype != NL_F32 && c_dtype != NL_BF16) return NL_ERR_DTYPE;
+  if (epi < NL_EPI_STORE || epi > NL_EPI_RESID) return NL_ERR_SHAPE;
+  if (epi == NL_EPI_ACCUM && c_dtype != NL_F32) return NL_ERR_DTYPE;
+  if (epi == NL_EPI_BIAS_GELU && (c_dtype != NL_BF16 || aux == nullptr)) return NL_ERR_DTYPE;
+  if (K == 0) {
+    if (epi == NL_EPI_ACCUM) return NL_OK;
+    return NL_ERR_SHAPE;
+  }
+  Params p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.C = Cp;
+  p.ldc = ldc;
+  p.c_bf16 = (c_dtype == NL_BF16);
+  p.epi = epi;
+  p.alpha = alpha;
+  p.bias = bias;
+  p.aux = reinterpret_cast<__nv_bfloat16*>(aux);
+  p.resid = resid;
+  p.err = device_error_word();
+  p.num_kb = (K + BK - 1) / BK;
+
+  const bool a_mn = a_trans != 0;
+  const bool b_mn = b_trans == 0;
+  // Narrow N gets 128-wide tiles (more CTAs); wide N gets 256-wide tiles.
+  const int sms = sm_count();
+  int BN = 256;
+  {
+    const long long t256 = (long long)((M + BM - 1) / BM) * ((N + 255) / 256);
+    if (N <= 128 || t256 < sms) BN = 128;
+  }
+  p.tiles_m = (M + BM - 1) / BM;
+  p.tiles_n = (N + BN - 1) / BN;
+  const int tiles = p.tiles_m * p.tiles_n;
+  // Split-K only for accumulate-mode GEMMs with few tiles and a long K.
+  p.split_k = 1;
+  if (epi == NL_EPI_ACCUM && tiles * 2 <= sms && p.num_kb >= 16) {
+    int s = sms / tiles;
+    s = s < p.num_kb / 8 ? s : p.num_kb / 8;
+    if (s < 1) s = 1;
+    p.split_k = s;
+  }
+  p.kb_per_split = (p.num_kb + p.split_k - 1) / p.split_k;
+  p.split_k = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
+
+  CUtensorMap ta, tb;
+  int st;
+  if (!a_mn) st = make_tmap_bf16_2d(&ta, A, K, M, lda, 64, BM);
+  else st = make_tmap_bf16_2d(&ta, A, M, K, lda, 64, BK);
+  if (st) return st;
+  if (!b_mn) st = make_tmap_bf16_2d(&tb, B, K, N, ldb, 64, BN);
+  else st = make_tmap_bf16_2d(&tb, B, N, K, ldb, 64, BK);
+  if (st) return st;
+
+  if (BN == 256) {
+    if (!a_mn && !b_mn) return launch<256, false, false>(ta, tb, p, stream);
+    if (!a_mn && b_mn) return launch<256, false, true>(ta, tb, p, stream);
+    if (a_mn && !b_mn) return launch<256, true, false>(ta, tb, p, stream);
+    return launch<256, true, true>(ta, tb, p, stream);
+  }
+  if (!a_mn && !b_mn) return launch<128, false, false>(ta, tb, p, stream);
+  if (!a_mn && b_mn) return launch<128, false, true>(ta, tb, p, stream);
+  if (a_mn && !b_mn) return launch<128, true, false>(ta, tb, p, stream);
+  return launch<128, true, true>(ta, tb, p, stream);
+}
+
+}  // namespace nl
+
+extern "C" int nl_gemm_ex(const void* A, int lda, int a_trans, const void* B, int ldb, int b_trans, void* C,
+                          int ldc, int c_dtype, int M, int N, int K, float alpha, int epilogue, const float* bias,
+                          void* aux, const void* resid, cudaStream_t stream) {
+  return nl::gemm_run(A, lda, a_trans, B, ldb, b_trans, C, ldc, c_dtype, M, N, K, alpha, epilogue, bias, aux,
+                      resid, stream);
+}
+
+extern "C" int nl_gemm(const void* A, const void* B, float* C, int M, int N, int K, cudaStream_t stream) {
+  return nl::gemm_run(A, K, 0, B, N, 0, C, N, NL_F32, M, N, K, 1.0f, NL_EPI_STORE, nullptr, nullptr, nullptr,
+                      stream);
+}

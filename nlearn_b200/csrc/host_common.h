@@ -1,0 +1,72 @@
+// host_common.h — host-side helpers shared by the C-ABI entry points:
+// TMA tensor-map encoding (driver entry point fetched through the runtime, so
+// the library does not link libcuda), SM count, and status codes.
+#pragma once
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/nl_ops.h"
+
+namespace nl {
+
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_tiled_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// Row-major bf16 matrix [rows, cols] with row pitch `ld` elements, tiled as
+// boxes of box_cols x box_rows with 128-byte swizzle (box_cols * 2 == 128).
+inline int make_tmap_bf16_2d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t ld,
+                             uint32_t box_cols, uint32_t box_rows) {
+  auto fn = encode_tiled_fn();
+  if (!fn) return NL_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * 2) & 15)) return NL_ERR_ALIGN;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NL_OK : NL_ERR_CUDA;
+}
+
+// Batched row-major bf16 tensor [batch, rows, cols] (contiguous), boxes of
+// box_cols x box_rows x 1 with 128-byte swizzle.  Rows past `rows` of one
+// batch entry read as zero instead of spilling into the next entry.
+inline int make_tmap_bf16_3d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t batch,
+                             uint32_t box_cols, uint32_t box_rows) {
+  auto fn = encode_tiled_fn();
+  if (!fn) return NL_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((cols * 2) & 15)) return NL_ERR_ALIGN;
+  cuuint64_t dims[3] = {cols, rows, batch};
+  cuuint64_t strides[2] = {cols * 2, cols * rows * 2};
+  cuuint32_t box[3] = {box_cols, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NL_OK : NL_ERR_CUDA;
+}
+
+inline int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? NL_OK : NL_ERR_LAUNCH;
+}
+
+}  // namespace nl
