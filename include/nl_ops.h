@@ -78,6 +78,56 @@ NL_API int nl_gemm_ex(const void* A, int lda, int a_trans, const void* B, int ld
                int c_dtype, int M, int N, int K, float alpha, int epilogue, const float* bias, void* aux,
                const void* resid, cudaStream_t stream);
 
+/* ---------------------------------------------------------------- cross-entropy
+ * Replaces targets `ce_fwd` / `ce_bwd` (nlearn/kernels/cross_entropy.py:28-46;
+ * iree_metal/kernels/cross_entropy.metal:38-68, 81-97).  logits [M,V] row-major
+ * with row pitch ld (any value >= V), dtype NL_F32 (the reference's) or NL_BF16;
+ * targets int32 [M].  A target outside [0,V) contributes loss = lse and no
+ * one-hot term.
+ *   nl_ce_fwd:     loss[M] = lse - logits[target], lse[M] = logsumexp(row)
+ *   nl_ce_bwd:     dlogits = (softmax(row) - onehot) * scale   (reference scale = 1/M)
+ *   nl_ce_fwd_bwd: both from one HBM read of the logits; dlogits may alias logits. */
+NL_API int nl_ce_fwd(const void* logits, long long ld, int in_dtype, const int* targets, float* loss, float* lse,
+                     int M, int V, cudaStream_t stream);
+NL_API int nl_ce_bwd(const void* logits, long long ld, int in_dtype, const int* targets, const float* lse,
+                     void* dlogits, long long ldd, int out_dtype, int M, int V, float scale, cudaStream_t stream);
+NL_API int nl_ce_fwd_bwd(const void* logits, long long ld, int in_dtype, const int* targets, float* loss,
+                         float* lse, void* dlogits, long long ldd, int out_dtype, int M, int V, float scale,
+                         cudaStream_t stream);
+
+/* ---------------------------------------------------------------- flash attention
+ * Causal attention over [n = batch*heads, s, d] row-major tensors, d == 64,
+ * scale 1/sqrt(d), any s >= 1.  Q/K/V/O/dO and the gradients are bf16 (the
+ * reference casts to f32 at its boundary, nlearn/attention.py:97; on B200 the
+ * tensor-core operands are bf16 and the caller casts); L and D are f32 [n,s].
+ *
+ * Replaces target `flash_attention_fwd` (nlearn/attention.py:82-91;
+ * iree_metal/kernels/flash_attention.metal:55-146): O, and L = logsumexp of the
+ * scaled scores (natural log) per query row. */
+NL_API int nl_flash_attention_fwd(const void* Q, const void* K, const void* V, void* O, float* L, int n, int s,
+                                  int d, cudaStream_t stream);
+
+/* Fused backward (one launch for dQ, dK, dV; nlearn/attention.py:111-128 calls
+ * the two reference targets below).  Computes D = rowsum(dO*O) into D_ws
+ * (f32 [n,s]) and accumulates dQ in dQacc_ws (f32 [n,s,64] scratch, any
+ * contents on entry: it is zeroed here). */
+NL_API int nl_flash_attention_bwd(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+                                  const float* L, float* D_ws, void* dQ, void* dK, void* dV, float* dQacc_ws, int n,
+                                  int s, int d, cudaStream_t stream);
+
+/* Replaces target `flash_attention_bwd_dq` (nlearn/attention.py:117-121;
+ * flash_attention.metal:168-243): dQ from Q,K,V,dO,L and the given D.
+ * dQacc_ws: f32 [n,s,64] scratch. */
+NL_API int nl_flash_attention_bwd_dq(const void* Q, const void* K, const void* V, const void* dO, const float* L,
+                                     const float* D, void* dQ, float* dQacc_ws, int n, int s, int d,
+                                     cudaStream_t stream);
+
+/* Replaces target `flash_attention_bwd_dkdv` (nlearn/attention.py:122-126;
+ * flash_attention.metal:265-347): dK, dV from Q,K,V,dO,L and the given D. */
+NL_API int nl_flash_attention_bwd_dkdv(const void* Q, const void* K, const void* V, const void* dO,
+                                       const float* L, const float* D, void* dK, void* dV, int n, int s, int d,
+                                       cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -29,6 +29,15 @@ SIGNATURES: dict[str, list] = {
     "nl_gemm": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
     "nl_gemm_ex": [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int,
                    c_float, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
+    "nl_ce_fwd": [c_void_p, c_longlong, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p],
+    "nl_ce_bwd": [c_void_p, c_longlong, c_int, c_void_p, c_void_p, c_void_p, c_longlong, c_int, c_int, c_int,
+                  c_float, c_void_p],
+    "nl_ce_fwd_bwd": [c_void_p, c_longlong, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_longlong, c_int,
+                      c_int, c_int, c_float, c_void_p],
+    "nl_flash_attention_fwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
+    "nl_flash_attention_bwd": [c_void_p] * 11 + [c_int, c_int, c_int, c_void_p],
+    "nl_flash_attention_bwd_dq": [c_void_p] * 8 + [c_int, c_int, c_int, c_void_p],
+    "nl_flash_attention_bwd_dkdv": [c_void_p] * 8 + [c_int, c_int, c_int, c_void_p],
 }
 _RESTYPE = {"nl_version": ctypes.c_char_p}
 

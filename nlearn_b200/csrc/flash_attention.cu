@@ -1,0 +1,729 @@
+// flash_attention.cu — causal FlashAttention forward + O(seq)-memory backward, sm_100a.
+//
+// Replaces nlearn's Metal kernels (iree_metal/kernels/flash_attention.metal):
+//   fwd       55-146  O = softmax(scale Q K^T + causal) V,  L = m + log(l)  (natural log)
+//   bwd_dq   168-243  dQ = scale sum_j p_ij (dP_ij - D_i) K_j
+//   bwd_dkdv 265-347  dV = P^T dO,  dK = scale dS^T Q
+// with p = exp(scale s - L) recomputed from L, D = rowsum(dO * O)
+// (nlearn/attention.py:116).  Layout [n = batch*heads, s, d=64], bf16 Q/K/V/O/dO,
+// f32 L and D, scale = 1/sqrt(64) (flash_attention.metal:64).
+//
+// Forward, one CTA per (head, 128-query tile), 6 warps, 2 CTAs per SM:
+//   warp 0     TMA: Q once, K_j / V_j into 2-slot rings
+//   warp 1     TMEM alloc (256 cols) + tcgen05.mma issuer:
+//                S = Q K_j^T  -> TMEM cols [0,128)    (M=128, N=128, K=64)
+//                O += P_j V_j -> TMEM cols [128,192)  (M=128, N=64,  K=128)
+//              S_{j+1} is issued as soon as the softmax warps have pulled S_j
+//              into registers, so it overlaps softmax_j.
+//   warps 2-5  softmax, one query row per thread: exp2-domain online softmax,
+//              O rescale in TMEM (tcgen05.ld/st) when the row max grows,
+//              P_j -> bf16 in shared memory in the UMMA K-major SW128 layout.
+// Causal tiles above the diagonal are never visited; heavy (late) query tiles
+// are scheduled first.
+//
+// Backward, one CTA per (head, 128-key tile), 10 warps, 1 CTA per SM:
+//   warp 0     TMA: K, V once; Q_i / dO_i into 2-slot rings
+//   warp 1     TMEM alloc (512 cols) + MMA issuer, per query tile i >= key tile:
+//                S^T  = K Q_i^T        cols [0,128)
+//                dP^T = V dO_i^T       cols [128,256)
+//                dV  += P^T dO_i       cols [256,320)   (B = dO_i read MN-major)
+//                dK  += dS^T Q_i       cols [320,384)   (B = Q_i  read MN-major)
+//                dQ_i = dS K           cols [384,448)   (A = dS^T read MN-major)
+//   warps 2-5  one key row per thread: P^T = exp2(S^T scale log2e - L log2e),
+//              dS^T = P^T (dP^T - D); both -> bf16 shared memory
+//   warps 6-9  dQ_i tile: TMEM -> float4 atomics into an f32 accumulator
+// followed by a convert kernel dQ = bf16(scale * dQacc).
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <math.h>
+
+#include "host_common.h"
+#include "sm100.cuh"
+
+namespace nl {
+namespace fa {
+
+constexpr int HD = 64;      // head dim (the reference's MAX_DHEAD, flash_attention.metal:17)
+constexpr int BQ = 128;     // query rows per tile
+constexpr int BKV = 128;    // key rows per tile
+constexpr int TILE = BQ * HD * 2;  // 16 KB bf16 tile
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// Byte offset of element (row r, col k) of a [rows x 128] bf16 matrix stored as
+// two K-major SW128 column halves of 16 KB each (the UMMA canonical layout the
+// TMA would produce), for 16-byte chunk index c8 = k / 8.
+__device__ __forceinline__ uint32_t sw128_off(int r, int c8) {
+  return (c8 >> 3) * 16384 + (r >> 3) * 1024 + (r & 7) * 128 + (((c8 & 7) ^ (r & 7)) << 4);
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ====================================================================== forward
+namespace fwd {
+constexpr int kThreads = 6 * 32;
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = TILE;           // 2 slots
+constexpr int OFF_V = 3 * TILE;       // 2 slots
+constexpr int OFF_P = 5 * TILE;       // 32 KB
+constexpr int OFF_BAR = 7 * TILE;
+constexpr int SMEM = OFF_BAR + 256;
+constexpr int TMEM_COLS = 256;
+constexpr int COL_S = 0, COL_O = 128;
+}  // namespace fwd
+
+struct FwdParams {
+  __nv_bfloat16* O;
+  float* L;
+  int n, s, nq;
+  float sl2;  // scale * log2(e)
+  int* err;
+};
+
+__global__ void __launch_bounds__(fwd::kThreads, 2)
+    flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, FwdParams p) {
+  using namespace fwd;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;
+  uint64_t* s_free = bars + 10;
+  uint64_t* p_full = bars + 11;
+  uint64_t* o_done = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id(), lane = lane_id();
+  // heavy (late) query tiles first
+  const int qb = p.nq - 1 - static_cast<int>(blockIdx.x) / p.n;
+  const int head = static_cast<int>(blockIdx.x) % p.n;
+  const int nkv = qb + 1;
+
+  if (smem_u32(smem) & 1023) {  // SW128 tiles need 1 KB alignment
+    if (threadIdx.x == 0 && p.err) atomicExch(p.err, 2);
+    return;
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 128);
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  Abort ab{abort_flag, p.err};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_expect_tx(q_full, TILE);
+      tma_load_3d(&tmQ, q_full, smem + OFF_Q, 0, qb * BQ, head);
+      for (int j = 0; j < nkv; ++j) {
+        const int slot = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&k_empty[slot], ph ^ 1, ab)) break;
+        mbar_expect_tx(&k_full[slot], TILE);
+        tma_load_3d(&tmK, &k_full[slot], smem + OFF_K + slot * TILE, 0, j * BKV, head);
+        if (!mbar_wait(&v_empty[slot], ph ^ 1, ab)) break;
+        mbar_expect_tx(&v_full[slot], TILE);
+        tma_load_3d(&tmV, &v_full[slot], smem + OFF_V + slot * TILE, 0, j * BKV, head);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(128, 128, 0, 0);
+      constexpr uint32_t idO = idesc_bf16_f32(128, 64, 0, 1);
+      const uint32_t sQ = smem_u32(smem + OFF_Q);
+      const uint32_t sP = smem_u32(smem + OFF_P);
+      bool ok = mbar_wait(q_full, 0, ab);
+      for (int j = 0; ok && j <= nkv; ++j) {
+        if (j < nkv) {
+          const int slot = j & 1;
+          if (!mbar_wait(&k_full[slot], (j >> 1) & 1, ab)) break;
+          if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, ab)) break;
+          tc_fence_after();
+          const uint32_t sK = smem_u32(smem + OFF_K + slot * TILE);
+#pragma unroll
+          for (int k = 0; k < HD / 16; ++k)
+            umma_f16_ss(tmem + COL_S, sdesc_sw128(sQ + k * 32, 16, 1024), sdesc_sw128(sK + k * 32, 16, 1024), idS,
+                        k > 0);
+          umma_commit(s_full);
+          umma_commit(&k_empty[slot]);
+        }
+        if (j > 0) {
+          const int jj = j - 1, slot = jj & 1;
+          if (!mbar_wait(p_full, jj & 1, ab)) break;
+          if (!mbar_wait(&v_full[slot], (jj >> 1) & 1, ab)) break;
+          tc_fence_after();
+          const uint32_t sV = smem_u32(smem + OFF_V + slot * TILE);
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk)
+            umma_f16_ss(tmem + COL_O, sdesc_sw128(sP + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                        sdesc_sw128(sV + kk * 2048, 8192, 1024), idO, (jj > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(o_done);
+          umma_commit(&v_empty[slot]);
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- softmax warps
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int q = qb * BQ + r;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t sP = smem_u32(smem + OFF_P);
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      if (!mbar_wait_warp(s_full, j & 1, ab)) { ok = false; break; }
+      tc_fence_after();
+      float sv[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t u[32];
+        tmem_ld32(trow + COL_S + c * 32, u);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) sv[c * 32 + e] = __uint_as_float(u[e]) * p.sl2;
+      }
+      tc_fence_before();
+      mbar_arrive(s_free);
+      if (j == qb) {  // diagonal tile: key index > query index is masked
+#pragma unroll
+        for (int e = 0; e < 128; ++e)
+          if (e > r) sv[e] = -INFINITY;
+      }
+      float mt = sv[0];
+#pragma unroll
+      for (int e = 1; e < 128; ++e) mt = fmaxf(mt, sv[e]);
+      const float m_new = fmaxf(m, mt);
+      float lt = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int e = 0; e < 64; ++e) {
+        const float a = ex2_approx(sv[2 * e] - m_new);
+        const float b = ex2_approx(sv[2 * e + 1] - m_new);
+        lt += a + b;
+        pk[e] = pack_bf16x2(a, b);
+      }
+      const float alpha = (j > 0) ? ex2_approx(m - m_new) : 0.f;
+      if (j > 0) {
+        // PV_{j-1} complete: P buffer free, O stable
+        if (!mbar_wait_warp(o_done, (j - 1) & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha < 1.f)) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t u[32];
+            tmem_ld32(trow + COL_O + c * 32, u);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
+            tmem_st32(trow + COL_O + c * 32, u);
+          }
+          tmem_wait_st();
+        }
+      }
+      l = l * alpha + lt;
+      m = m_new;
+#pragma unroll
+      for (int c8 = 0; c8 < 16; ++c8)
+        st_shared_v4(sP + sw128_off(r, c8), pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait_warp(o_done, (nkv - 1) & 1, ab)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      uint32_t ov[32];
+      __nv_bfloat16* orow = p.O + ((long long)head * p.s + q) * HD;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t u[32];
+        tmem_ld32(trow + COL_O + c * 32, u);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          ov[e] = pack_bf16x2(__uint_as_float(u[2 * e]) * inv, __uint_as_float(u[2 * e + 1]) * inv);
+        if (q < p.s) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) dst[v] = make_uint4(ov[4 * v], ov[4 * v + 1], ov[4 * v + 2], ov[4 * v + 3]);
+        }
+      }
+      if (q < p.s) p.L[(long long)head * p.s + q] = (m + __log2f(l)) * kLn2;
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// ====================================================================== backward
+namespace bwd {
+constexpr int kThreads = 10 * 32;
+constexpr int OFF_K = 0;
+constexpr int OFF_V = TILE;
+constexpr int OFF_Q = 2 * TILE;   // 2 slots
+constexpr int OFF_DO = 4 * TILE;  // 2 slots
+constexpr int OFF_P = 6 * TILE;   // 32 KB  P^T  [kv rows, q cols]
+constexpr int OFF_DS = 8 * TILE;  // 32 KB  dS^T [kv rows, q cols]
+constexpr int OFF_LD = 10 * TILE; // L2[2][128], D[2][128] f32
+constexpr int OFF_BAR = OFF_LD + 2048;
+constexpr int SMEM = OFF_BAR + 256;
+constexpr int TMEM_COLS = 512;
+constexpr int COL_S = 0, COL_DP = 128, COL_DV = 256, COL_DK = 320, COL_DQ = 384;
+}  // namespace bwd
+
+struct BwdParams {
+  const float* L;  // natural-log LSE [n, s]
+  const float* D;  // rowsum(dO * O)  [n, s]
+  float* dQacc;    // [n, s, 64] f32, zeroed
+  __nv_bfloat16* dK;
+  __nv_bfloat16* dV;
+  int n, s, nq;
+  float sl2, scale;
+  int want_dq, want_dkdv;
+  int* err;
+};
+
+__global__ void __launch_bounds__(bwd::kThreads, 1)
+    flash_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                     BwdParams p) {
+  using namespace bwd;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;   // [2]
+  uint64_t* qdo_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* st_free = bars + 6;
+  uint64_t* ds_full = bars + 7;
+  uint64_t* ds_empty = bars + 8;
+  uint64_t* dq_full = bars + 9;
+  uint64_t* dq_free = bars + 10;
+  uint64_t* acc_done = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* Lbuf = reinterpret_cast<float*>(smem + OFF_LD);  // [2][128]
+  float* Dbuf = Lbuf + 256;                               // [2][128]
+
+  const int warp = warp_id(), lane = lane_id();
+  const int jb = static_cast<int>(blockIdx.x) / p.n;  // key tile; jb = 0 has the most work
+  const int head = static_cast<int>(blockIdx.x) % p.n;
+  const int n_it = p.nq - jb;
+
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0 && p.err) atomicExch(p.err, 2);
+    return;
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(st_free, 128);
+    mbar_init(ds_full, 128);
+    mbar_init(ds_empty, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 128);
+    mbar_init(acc_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  Abort ab{abort_flag, p.err};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmDO);
+      mbar_expect_tx(kv_full, 2 * TILE);
+      tma_load_3d(&tmK, kv_full, smem + OFF_K, 0, jb * BKV, head);
+      tma_load_3d(&tmV, kv_full, smem + OFF_V, 0, jb * BKV, head);
+      for (int it = 0; it < n_it; ++it) {
+        const int slot = it & 1, i = jb + it;
+        if (!mbar_wait(&qdo_empty[slot], ((it >> 1) & 1) ^ 1, ab)) break;
+        mbar_expect_tx(&qdo_full[slot], 2 * TILE);
+        tma_load_3d(&tmQ, &qdo_full[slot], smem + OFF_Q + slot * TILE, 0, i * BQ, head);
+        tma_load_3d(&tmDO, &qdo_full[slot], smem + OFF_DO + slot * TILE, 0, i * BQ, head);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(128, 128, 0, 0);   // S^T, dP^T
+      constexpr uint32_t idKV = idesc_bf16_f32(128, 64, 0, 1);   // dV, dK: B MN-major
+      constexpr uint32_t idQ = idesc_bf16_f32(128, 64, 1, 1);    // dQ: A and B MN-major
+      const uint32_t sK = smem_u32(smem + OFF_K), sV = smem_u32(smem + OFF_V);
+      const uint32_t sP = smem_u32(smem + OFF_P), sDS = smem_u32(smem + OFF_DS);
+      bool ok = mbar_wait(kv_full, 0, ab);
+      for (int it = 0; ok && it < n_it; ++it) {
+        const int slot = it & 1;
+        if (!mbar_wait(&qdo_full[slot], (it >> 1) & 1, ab)) { ok = false; break; }
+        if (it > 0 && !mbar_wait(st_free, (it - 1) & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sQ = smem_u32(smem + OFF_Q + slot * TILE);
+        const uint32_t sDO = smem_u32(smem + OFF_DO + slot * TILE);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k)
+          umma_f16_ss(tmem + COL_S, sdesc_sw128(sK + k * 32, 16, 1024), sdesc_sw128(sQ + k * 32, 16, 1024), idS,
+                      k > 0);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k)
+          umma_f16_ss(tmem + COL_DP, sdesc_sw128(sV + k * 32, 16, 1024), sdesc_sw128(sDO + k * 32, 16, 1024), idS,
+                      k > 0);
+        umma_commit(s_full);
+        if (!mbar_wait(ds_full, it & 1, ab)) { ok = false; break; }
+        tc_fence_after();
+        if (p.want_dkdv) {
+#pragma unroll
+          for (int kk = 0; kk < BQ / 16; ++kk) {
+            const uint32_t a_off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_f16_ss(tmem + COL_DV, sdesc_sw128(sP + a_off, 16, 1024), sdesc_sw128(sDO + kk * 2048, 8192, 1024),
+                        idKV, (it > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_ss(tmem + COL_DK, sdesc_sw128(sDS + a_off, 16, 1024), sdesc_sw128(sQ + kk * 2048, 8192, 1024),
+                        idKV, (it > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        if (p.want_dq) {
+          if (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk)
+            umma_f16_ss(tmem + COL_DQ, sdesc_sw128(sDS + kk * 2048, 16384, 1024),
+                        sdesc_sw128(sK + kk * 2048, 8192, 1024), idQ, kk > 0 ? 1u : 0u);
+          umma_commit(dq_full);
+        }
+        umma_commit(ds_empty);
+        umma_commit(&qdo_empty[slot]);
+      }
+      if (ok) umma_commit(acc_done);
+    }
+  } else if (warp < 6) {
+    // ---------------------------------------------------------- P / dS warps (one key row each)
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int t = (warp - 2) * 32 + lane;  // 0..127 loader index
+    const int kv = jb * BKV + r;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t sP = smem_u32(smem + OFF_P), sDS = smem_u32(smem + OFF_DS);
+    const float* Lh = p.L + (long long)head * p.s;
+    const float* Dh = p.D + (long long)head * p.s;
+    float l_next, d_next;
+    {
+      const int qi = jb * BQ + t;
+      l_next = (qi < p.s) ? Lh[qi] * kLog2e : INFINITY;
+      d_next = (qi < p.s) ? Dh[qi] : 0.f;
+    }
+    // On a timeout the loop keeps iterating without work so that all 128
+    // threads still meet at every named barrier (a barrier can not time out).
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int i = jb + it, buf = it & 1;
+      Lbuf[buf * 128 + t] = l_next;
+      Dbuf[buf * 128 + t] = d_next;
+      named_bar_sync(1, 128);
+      if (it + 1 < n_it) {
+        const int qi = (i + 1) * BQ + t;
+        l_next = (qi < p.s) ? Lh[qi] * kLog2e : INFINITY;
+        d_next = (qi < p.s) ? Dh[qi] : 0.f;
+      }
+      if (ok) ok = mbar_wait_warp(s_full, it & 1, ab);
+      if (ok && it > 0) ok = mbar_wait_warp(ds_empty, (it - 1) & 1, ab);
+      if (!ok) continue;
+      tc_fence_after();
+      const float* Lb = Lbuf + buf * 128;
+      const float* Db = Dbuf + buf * 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t us[32], ud[32];
+        tmem_ld32(trow + COL_S + c * 32, us);
+        tmem_ld32(trow + COL_DP + c * 32, ud);
+        tmem_wait_ld();
+        uint32_t pp[16], dd[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int qc = c * 32 + e + h;
+            const int qg = i * BQ + qc;
+            float pr = ex2_approx(__uint_as_float(us[e + h]) * p.sl2 - Lb[qc]);
+            pr = (qg >= kv && qg < p.s) ? pr : 0.f;  // causal (query >= key), in range
+            pv[h] = pr;
+            dv[h] = pr * (__uint_as_float(ud[e + h]) - Db[qc]);
+          }
+          pp[e / 2] = pack_bf16x2(pv[0], pv[1]);
+          dd[e / 2] = pack_bf16x2(dv[0], dv[1]);
+        }
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const uint32_t off = sw128_off(r, c * 4 + v);
+          st_shared_v4(sP + off, pp[4 * v], pp[4 * v + 1], pp[4 * v + 2], pp[4 * v + 3]);
+          st_shared_v4(sDS + off, dd[4 * v], dd[4 * v + 1], dd[4 * v + 2], dd[4 * v + 3]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(st_free);
+      fence_proxy_async_smem();
+      mbar_arrive(ds_full);
+    }
+    if (ok && p.want_dkdv && mbar_wait_warp(acc_done, 0, ab)) {
+      tc_fence_after();
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        __nv_bfloat16* dst = (which == 0 ? p.dV : p.dK) + ((long long)head * p.s + kv) * HD;
+        const float mul = (which == 0) ? 1.f : p.scale;
+        const uint32_t col = (which == 0) ? COL_DV : COL_DK;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t u[32];
+          tmem_ld32(trow + col + c * 32, u);
+          tmem_wait_ld();
+          if (kv < p.s) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              d4[v] = make_uint4(pack_bf16x2(__uint_as_float(u[8 * v + 0]) * mul, __uint_as_float(u[8 * v + 1]) * mul),
+                                 pack_bf16x2(__uint_as_float(u[8 * v + 2]) * mul, __uint_as_float(u[8 * v + 3]) * mul),
+                                 pack_bf16x2(__uint_as_float(u[8 * v + 4]) * mul, __uint_as_float(u[8 * v + 5]) * mul),
+                                 pack_bf16x2(__uint_as_float(u[8 * v + 6]) * mul, __uint_as_float(u[8 * v + 7]) * mul));
+          }
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- dQ warps (one query row each)
+    if (p.want_dq) {
+      const int quarter = warp & 3;
+      const int r = quarter * 32 + lane;
+      const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+      for (int it = 0; it < n_it; ++it) {
+        const int q = (jb + it) * BQ + r;
+        if (!mbar_wait_warp(dq_full, it & 1, ab)) break;
+        tc_fence_after();
+        uint32_t u0[32], u1[32];
+        tmem_ld32(trow + COL_DQ, u0);
+        tmem_ld32(trow + COL_DQ + 32, u1);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(dq_free);
+        if (q < p.s) {
+          float4* dst = reinterpret_cast<float4*>(p.dQacc + ((long long)head * p.s + q) * HD);
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            atomicAdd(dst + v, make_float4(__uint_as_float(u0[4 * v]), __uint_as_float(u0[4 * v + 1]),
+                                           __uint_as_float(u0[4 * v + 2]), __uint_as_float(u0[4 * v + 3])));
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            atomicAdd(dst + 8 + v, make_float4(__uint_as_float(u1[4 * v]), __uint_as_float(u1[4 * v + 1]),
+                                               __uint_as_float(u1[4 * v + 2]), __uint_as_float(u1[4 * v + 3])));
+        }
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// D[row] = sum_d dO[row,d] * O[row,d]; optionally zero the dQ accumulator row.
+// One warp per row (64 bf16 = 32 bf16x2).
+__global__ void bwd_preprocess_kernel(const __nv_bfloat16* __restrict__ O, const __nv_bfloat16* __restrict__ dO,
+                                      float* __restrict__ D, float* __restrict__ dQacc, long long rows) {
+  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float acc = 0.f;
+  if (O != nullptr) {
+    const __nv_bfloat162 o = reinterpret_cast<const __nv_bfloat162*>(O + row * HD)[lane];
+    const __nv_bfloat162 g = reinterpret_cast<const __nv_bfloat162*>(dO + row * HD)[lane];
+    const float2 of = __bfloat1622float2(o), gf = __bfloat1622float2(g);
+    acc = of.x * gf.x + of.y * gf.y;
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o2);
+    if (lane == 0) D[row] = acc;
+  }
+  if (dQacc) reinterpret_cast<float2*>(dQacc + row * HD)[lane] = make_float2(0.f, 0.f);
+}
+
+__global__ void dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dQ, float scale,
+                                  long long n4) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n4) return;
+  const float4 v = reinterpret_cast<const float4*>(acc)[i];
+  reinterpret_cast<uint2*>(dQ)[i] = make_uint2(pack_bf16x2(v.x * scale, v.y * scale), pack_bf16x2(v.z * scale, v.w * scale));
+}
+
+static int check_common(const void* Q, const void* K, const void* V, int n, int s, int d) {
+  if (n <= 0 || s <= 0) return NL_ERR_SHAPE;
+  if (d != HD) return NL_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(Q) | reinterpret_cast<uintptr_t>(K) | reinterpret_cast<uintptr_t>(V)) & 15)
+    return NL_ERR_ALIGN;
+  return NL_OK;
+}
+
+template <typename Kern>
+static int set_smem(Kern k, int bytes) {
+  static int dev_done = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev_done == dev) return NL_OK;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return NL_ERR_LAUNCH;
+  dev_done = dev;
+  return NL_OK;
+}
+
+}  // namespace fa
+
+int* device_error_word();
+
+int flash_fwd(const void* Q, const void* K, const void* V, void* O, float* L, int n, int s, int d,
+              cudaStream_t stream) {
+  using namespace fa;
+  int st = check_common(Q, K, V, n, s, d);
+  if (st) return st;
+  if (reinterpret_cast<uintptr_t>(O) & 15) return NL_ERR_ALIGN;
+  CUtensorMap tq, tk, tv;
+  if ((st = make_tmap_bf16_3d(&tq, Q, HD, s, n, 64, BQ))) return st;
+  if ((st = make_tmap_bf16_3d(&tk, K, HD, s, n, 64, BKV))) return st;
+  if ((st = make_tmap_bf16_3d(&tv, V, HD, s, n, 64, BKV))) return st;
+  FwdParams p{};
+  p.O = reinterpret_cast<__nv_bfloat16*>(O);
+  p.L = L;
+  p.n = n;
+  p.s = s;
+  p.nq = (s + BQ - 1) / BQ;
+  p.sl2 = (1.f / sqrtf(static_cast<float>(HD))) * kLog2e;
+  p.err = device_error_word();
+  if ((st = set_smem(flash_fwd_kernel, fwd::SMEM))) return st;
+  const long long grid = static_cast<long long>(n) * p.nq;
+  if (grid > 0x7fffffffLL) return NL_ERR_SHAPE;
+  flash_fwd_kernel<<<static_cast<unsigned>(grid), fwd::kThreads, fwd::SMEM, stream>>>(tq, tk, tv, p);
+  return launch_status();
+}
+
+// Full backward.  D (f32 [n,s]) and dQacc (f32 [n,s,64]) are caller workspaces;
+// if O is non-null, D is computed here from O and dO, otherwise D is an input.
+int flash_bwd(const void* Q, const void* K, const void* V, const void* O, const void* dO, const float* L,
+              float* D, void* dQ, void* dK, void* dV, float* dQacc, int n, int s, int d, cudaStream_t stream) {
+  using namespace fa;
+  int st = check_common(Q, K, V, n, s, d);
+  if (st) return st;
+  if (!dO || !L || !D) return NL_ERR_SHAPE;
+  const bool want_dq = dQ != nullptr;
+  const bool want_dkdv = dK != nullptr && dV != nullptr;
+  if (want_dq && !dQacc) return NL_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(dO) | reinterpret_cast<uintptr_t>(dQ) | reinterpret_cast<uintptr_t>(dK) |
+       reinterpret_cast<uintptr_t>(dV) | reinterpret_cast<uintptr_t>(dQacc)) & 15)
+    return NL_ERR_ALIGN;
+  const long long rows = static_cast<long long>(n) * s;
+  if (O || want_dq) {
+    const long long threads = rows * 32;
+    bwd_preprocess_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(O), reinterpret_cast<const __nv_bfloat16*>(dO), D,
+        want_dq ? dQacc : nullptr, rows);
+    if ((st = launch_status())) return st;
+  }
+  CUtensorMap tq, tk, tv, tdo;
+  if ((st = make_tmap_bf16_3d(&tq, Q, HD, s, n, 64, BQ))) return st;
+  if ((st = make_tmap_bf16_3d(&tk, K, HD, s, n, 64, BKV))) return st;
+  if ((st = make_tmap_bf16_3d(&tv, V, HD, s, n, 64, BKV))) return st;
+  if ((st = make_tmap_bf16_3d(&tdo, dO, HD, s, n, 64, BQ))) return st;
+  BwdParams p{};
+  p.L = L;
+  p.D = D;
+  p.dQacc = dQacc;
+  p.dK = reinterpret_cast<__nv_bfloat16*>(dK);
+  p.dV = reinterpret_cast<__nv_bfloat16*>(dV);
+  p.n = n;
+  p.s = s;
+  p.nq = (s + BQ - 1) / BQ;
+  p.scale = 1.f / sqrtf(static_cast<float>(HD));
+  p.sl2 = p.scale * kLog2e;
+  p.want_dq = want_dq;
+  p.want_dkdv = want_dkdv;
+  p.err = device_error_word();
+  if ((st = set_smem(flash_bwd_kernel, bwd::SMEM))) return st;
+  const long long grid = static_cast<long long>(n) * p.nq;
+  flash_bwd_kernel<<<static_cast<unsigned>(grid), bwd::kThreads, bwd::SMEM, stream>>>(tq, tk, tv, tdo, p);
+  if ((st = launch_status())) return st;
+  if (want_dq) {
+    const long long n4 = rows * HD / 4;
+    dq_convert_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, stream>>>(
+        dQacc, reinterpret_cast<__nv_bfloat16*>(dQ), p.scale, n4);
+    if ((st = launch_status())) return st;
+  }
+  return NL_OK;
+}
+
+}  // namespace nl
+
+extern "C" int nl_flash_attention_fwd(const void* Q, const void* K, const void* V, void* O, float* L, int n, int s,
+                                      int d, cudaStream_t stream) {
+  return nl::flash_fwd(Q, K, V, O, L, n, s, d, stream);
+}
+
+extern "C" int nl_flash_attention_bwd(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+                                      const float* L, float* D_ws, void* dQ, void* dK, void* dV, float* dQacc_ws,
+                                      int n, int s, int d, cudaStream_t stream) {
+  if (!O) return NL_ERR_SHAPE;
+  return nl::flash_bwd(Q, K, V, O, dO, L, D_ws, dQ, dK, dV, dQacc_ws, n, s, d, stream);
+}
+
+extern "C" int nl_flash_attention_bwd_dq(const void* Q, const void* K, const void* V, const void* dO,
+                                         const float* L, const float* D, void* dQ, float* dQacc_ws, int n, int s,
+                                         int d, cudaStream_t stream) {
+  if (!dQ) return NL_ERR_SHAPE;
+  return nl::flash_bwd(Q, K, V, nullptr, dO, L, const_cast<float*>(D), dQ, nullptr, nullptr, dQacc_ws, n, s, d,
+                       stream);
+}
+
+extern "C" int nl_flash_attention_bwd_dkdv(const void* Q, const void* K, const void* V, const void* dO,
+                                           const float* L, const float* D, void* dK, void* dV, int n, int s, int d,
+                                           cudaStream_t stream) {
+  if (!dK || !dV) return NL_ERR_SHAPE;
+  return nl::flash_bwd(Q, K, V, nullptr, dO, L, const_cast<float*>(D), nullptr, dK, dV, nullptr, n, s, d, stream);
+}

@@ -83,6 +83,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   return false;
 }
 
+// Warp-uniform variant for consumers that go on to issue warp-collective
+// (.sync.aligned) tcgen05.ld/st: every lane waits, and the result is the AND
+// over the warp so that no lane proceeds alone.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, const Abort& ab) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, ab));
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");

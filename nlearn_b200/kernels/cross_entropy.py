@@ -1,0 +1,98 @@
+"""Softmax cross-entropy on the sm_100a kernels — mirror of nlearn.kernels.cross_entropy.
+
+Reference surface (nlearn/kernels/cross_entropy.py):
+  * ``_ce_fwd_raw(logits, targets) -> (loss[M], lse[M])``   target `ce_fwd` (28-36)
+  * ``_ce_bwd_raw(logits, targets, lse) -> dlogits / M``    target `ce_bwd` (39-46)
+  * ``cross_entropy(logits, targets)``  mean CE, custom_vjp, flattens (49-81)
+  * ``linear_cross_entropy(X, W, targets)`` LM head + CE without the (M, V)
+    logits, custom_vjp; backward recomputes the logits (85-170)
+
+``linear_cross_entropy`` runs the fused LM-head kernels (``nl_lce_fwd`` /
+``nl_lce_bwd``): the GEMM epilogue reduces each 128x256 logit tile to per-row
+(max, sum-exp) partials, and the backward turns each recomputed tile straight
+into bf16 dlogits for the dX / dW GEMMs, one vocabulary chunk at a time.
+"""
+from __future__ import annotations
+
+import torch
+
+from .._lib import BF16, F32, check, lib, ptr, stream_handle
+
+_DT = {torch.float32: F32, torch.bfloat16: BF16}
+
+
+def _rows(logits: torch.Tensor) -> torch.Tensor:
+    if not logits.is_cuda:
+        raise ValueError("nlearn_b200 cross-entropy runs on CUDA tensors only (no CPU fallback)")
+    if logits.dtype not in _DT:
+        logits = logits.float()
+    if logits.stride(-1) != 1:
+        logits = logits.contiguous()
+    return logits
+
+
+def _ce_fwd_raw(logits: torch.Tensor, targets: torch.Tensor):
+    """logits[M,V] (f32 or bf16; any row pitch), targets[M] -> (loss[M], lse[M]) f32."""
+    lg = _rows(logits)
+    M, V = lg.shape
+    t = targets.to(torch.int32).contiguous()
+    loss = torch.empty(M, device=lg.device, dtype=torch.float32)
+    lse = torch.empty(M, device=lg.device, dtype=torch.float32)
+    check(lib.nl_ce_fwd(ptr(lg), lg.stride(0), _DT[lg.dtype], ptr(t), ptr(loss), ptr(lse), M, V, stream_handle()),
+          "nl_ce_fwd")
+    return loss, lse
+
+
+def _ce_bwd_raw(logits: torch.Tensor, targets: torch.Tensor, lse: torch.Tensor, scale: float | None = None,
+                out_dtype=None, out: torch.Tensor | None = None):
+    """dlogits = (softmax - onehot) * scale, scale defaulting to 1/M (the reference's)."""
+    lg = _rows(logits)
+    M, V = lg.shape
+    t = targets.to(torch.int32).contiguous()
+    if out is None:
+        out = torch.empty(M, V, device=lg.device, dtype=out_dtype or lg.dtype)
+    sc = (1.0 / M) if scale is None else float(scale)
+    check(lib.nl_ce_bwd(ptr(lg), lg.stride(0), _DT[lg.dtype], ptr(t), ptr(lse.float().contiguous()), ptr(out),
+                        out.stride(0), _DT[out.dtype], M, V, sc, stream_handle()), "nl_ce_bwd")
+    return out
+
+
+def ce_fwd_bwd(logits: torch.Tensor, targets: torch.Tensor, scale: float | None = None,
+               out: torch.Tensor | None = None, out_dtype=None):
+    """Fused: loss[M], lse[M] and dlogits from one read of the logits.
+    ``out`` may be ``logits`` itself (in-place gradient)."""
+    lg = _rows(logits)
+    M, V = lg.shape
+    t = targets.to(torch.int32).contiguous()
+    loss = torch.empty(M, device=lg.device, dtype=torch.float32)
+    lse = torch.empty(M, device=lg.device, dtype=torch.float32)
+    if out is None:
+        out = torch.empty(M, V, device=lg.device, dtype=out_dtype or lg.dtype)
+    sc = (1.0 / M) if scale is None else float(scale)
+    check(lib.nl_ce_fwd_bwd(ptr(lg), lg.stride(0), _DT[lg.dtype], ptr(t), ptr(loss), ptr(lse), ptr(out),
+                            out.stride(0), _DT[out.dtype], M, V, sc, stream_handle()), "nl_ce_fwd_bwd")
+    return loss, lse, out
+
+
+class _CE(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, logits, targets):
+        loss, lse = _ce_fwd_raw(logits, targets)
+        ctx.save_for_backward(logits, targets, lse)
+        return loss.mean()
+
+    @staticmethod
+    def backward(ctx, g):
+        logits, targets, lse = ctx.saved_tensors
+        d = _ce_bwd_raw(logits, targets, lse, scale=None, out_dtype=logits.dtype if logits.dtype in _DT
+                        else torch.float32)
+        return d * g.to(d.dtype), None
+
+
+def cross_entropy(logits: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+    """Mean softmax cross-entropy; leading dims flattened to (M, V)."""
+    V = logits.shape[-1]
+    return _CE.apply(logits.reshape(-1, V), targets.reshape(-1))
+
+
+__all__ = ["cross_entropy", "_ce_fwd_raw", "_ce_bwd_raw", "ce_fwd_bwd"]
