@@ -50,7 +50,9 @@ typedef enum {
   NL_EPI_ACCUM = 1,     /* C += alpha*A.B                (C f32; split-K safe) */
   NL_EPI_BIAS = 2,      /* C = alpha*A.B + bias[N]       (bias f32)            */
   NL_EPI_BIAS_GELU = 3, /* aux = A.B + bias; C = gelu_tanh(aux)  (C, aux bf16) */
-  NL_EPI_RESID = 4      /* C = alpha*A.B + bias? + resid (resid in c_dtype)    */
+  NL_EPI_RESID = 4,     /* C = alpha*A.B + bias? + resid (resid in c_dtype)    */
+  NL_EPI_LCE_STATS = 5, /* internal: fused LM-head CE partial row statistics   */
+  NL_EPI_LCE_GRAD = 6   /* internal: fused LM-head CE dlogits (bf16)           */
 } nl_epilogue;
 
 /* Library / device introspection. */
@@ -127,6 +129,42 @@ NL_API int nl_flash_attention_bwd_dq(const void* Q, const void* K, const void* V
 NL_API int nl_flash_attention_bwd_dkdv(const void* Q, const void* K, const void* V, const void* dO,
                                        const float* L, const float* D, void* dK, void* dV, int n, int s, int d,
                                        cudaStream_t stream);
+
+/* Strided forms used by the training step: activations addressed as
+ * [B][H][s][64] with element strides (q_s, q_h, q_b) for Q, K, V, dQ, dK, dV
+ * and (o_s, o_h, o_b) for O, dO — e.g. Q/K/V read in place from a fused QKV
+ * projection [B, s, 3, H, 64] and O written as [B, s, H, 64].  Strides must be
+ * multiples of 8 elements.  L, D_ws: f32 [B*H, s]; dQacc_ws: f32 [B*H, s, 64].
+ * No reference counterpart: nlearn permutes to (B*H, s, 64) in JAX
+ * (nlearn/model.py:175-181) before the contiguous targets above. */
+NL_API int nl_flash_attention_fwd_strided(const void* Q, const void* K, const void* V, long long q_s, long long q_h,
+                                          long long q_b, void* O, long long o_s, long long o_h, long long o_b,
+                                          float* L, int B, int H, int s, int d, cudaStream_t stream);
+NL_API int nl_flash_attention_bwd_strided(const void* Q, const void* K, const void* V, long long q_s, long long q_h,
+                                          long long q_b, const void* O, const void* dO, long long o_s, long long o_h,
+                                          long long o_b, const float* L, float* D_ws, void* dQ, void* dK, void* dV,
+                                          float* dQacc_ws, int B, int H, int s, int d, cudaStream_t stream);
+
+/* ---------------------------------------------------------------- fused LM-head CE
+ * Replaces the jnp-chunked `linear_cross_entropy` (nlearn/kernels/
+ * cross_entropy.py:106-167; its custom_vjp 131-170): loss over
+ * logits = X[M,D] . W[D,V] (bf16, row-major, ldx/ldw multiples of 8, ldw >= V)
+ * without materialising the logits.  Workspace (caller-owned, 256-byte
+ * aligned): nl_lce_workspace_bytes(M, V, 0) for the forward,
+ * nl_lce_workspace_bytes(M, V, chunk) for the backward. */
+NL_API size_t nl_lce_workspace_bytes(int M, int V, int chunk);
+
+/* loss[M] = lse - logit[target], lse[M] (f32). */
+NL_API int nl_lce_fwd(const void* X, int ldx, const void* W, int ldw, const int* targets, float* loss, float* lse,
+                      void* workspace, size_t ws_bytes, int M, int D, int V, cudaStream_t stream);
+
+/* dlogits = (softmax - onehot) * grad_mul * (*gscale if gscale != NULL), per
+ * vocabulary chunk (chunk % 64 == 0):  dX[M,D] f32 += dlogits . W^T (caller
+ * zeroes dX, or passes existing gradients to accumulate);
+ * dW[D,V] f32 (row pitch lddw) = X^T . dlogits, or += when dw_accumulate. */
+NL_API int nl_lce_bwd(const void* X, int ldx, const void* W, int ldw, const int* targets, const float* lse,
+                      const float* gscale, float grad_mul, float* dX, float* dW, int lddw, int dw_accumulate,
+                      void* workspace, size_t ws_bytes, int chunk, int M, int D, int V, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -38,8 +38,17 @@ SIGNATURES: dict[str, list] = {
     "nl_flash_attention_bwd": [c_void_p] * 11 + [c_int, c_int, c_int, c_void_p],
     "nl_flash_attention_bwd_dq": [c_void_p] * 8 + [c_int, c_int, c_int, c_void_p],
     "nl_flash_attention_bwd_dkdv": [c_void_p] * 8 + [c_int, c_int, c_int, c_void_p],
+    "nl_flash_attention_fwd_strided": [c_void_p] * 3 + [c_longlong] * 3 + [c_void_p] + [c_longlong] * 3 +
+                                      [c_void_p, c_int, c_int, c_int, c_int, c_void_p],
+    "nl_flash_attention_bwd_strided": [c_void_p] * 3 + [c_longlong] * 3 + [c_void_p] * 2 + [c_longlong] * 3 +
+                                      [c_void_p] * 6 + [c_int, c_int, c_int, c_int, c_void_p],
+    "nl_lce_workspace_bytes": [c_int, c_int, c_int],
+    "nl_lce_fwd": [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t,
+                   c_int, c_int, c_int, c_void_p],
+    "nl_lce_bwd": [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
+                   c_int, c_int, c_void_p, ctypes.c_size_t, c_int, c_int, c_int, c_int, c_void_p],
 }
-_RESTYPE = {"nl_version": ctypes.c_char_p}
+_RESTYPE = {"nl_version": ctypes.c_char_p, "nl_lce_workspace_bytes": ctypes.c_size_t}
 
 
 class NlError(RuntimeError):

@@ -78,10 +78,18 @@ constexpr int TMEM_COLS = 256;
 constexpr int COL_S = 0, COL_O = 128;
 }  // namespace fwd
 
+// Activations are addressed as [b][h][s][64] with element strides, so Q/K/V
+// can be read straight out of a fused QKV projection and O written in the
+// layout the output projection consumes (no permute copies).
+struct Strides {
+  long long s, h, b;
+};
+
 struct FwdParams {
   __nv_bfloat16* O;
+  Strides os;
   float* L;
-  int n, s, nq;
+  int n, H, s, nq;
   float sl2;  // scale * log2(e)
   int* err;
 };
@@ -107,7 +115,8 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
   const int warp = warp_id(), lane = lane_id();
   // heavy (late) query tiles first
   const int qb = p.nq - 1 - static_cast<int>(blockIdx.x) / p.n;
-  const int head = static_cast<int>(blockIdx.x) % p.n;
+  const int head = static_cast<int>(blockIdx.x) % p.n;  // = bi * H + hi
+  const int bi = head / p.H, hi = head % p.H;
   const int nkv = qb + 1;
 
   if (smem_u32(smem) & 1023) {  // SW128 tiles need 1 KB alignment
@@ -142,16 +151,16 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       mbar_expect_tx(q_full, TILE);
-      tma_load_3d(&tmQ, q_full, smem + OFF_Q, 0, qb * BQ, head);
+      tma_load_4d(&tmQ, q_full, smem + OFF_Q, 0, qb * BQ, hi, bi);
       for (int j = 0; j < nkv; ++j) {
         const int slot = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait(&k_empty[slot], ph ^ 1, ab)) break;
         mbar_expect_tx(&k_full[slot], TILE);
-        tma_load_3d(&tmK, &k_full[slot], smem + OFF_K + slot * TILE, 0, j * BKV, head);
+        tma_load_4d(&tmK, &k_full[slot], smem + OFF_K + slot * TILE, 0, j * BKV, hi, bi);
         if (!mbar_wait(&v_empty[slot], ph ^ 1, ab)) break;
         mbar_expect_tx(&v_full[slot], TILE);
-        tma_load_3d(&tmV, &v_full[slot], smem + OFF_V + slot * TILE, 0, j * BKV, head);
+        tma_load_4d(&tmV, &v_full[slot], smem + OFF_V + slot * TILE, 0, j * BKV, hi, bi);
       }
     }
   } else if (warp == 1) {
@@ -262,7 +271,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
       tc_fence_after();
       const float inv = 1.f / l;
       uint32_t ov[32];
-      __nv_bfloat16* orow = p.O + ((long long)head * p.s + q) * HD;
+      __nv_bfloat16* orow = p.O + bi * p.os.b + q * p.os.s + hi * p.os.h;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t u[32];
@@ -310,7 +319,8 @@ struct BwdParams {
   float* dQacc;    // [n, s, 64] f32, zeroed
   __nv_bfloat16* dK;
   __nv_bfloat16* dV;
-  int n, s, nq;
+  Strides gs;  // strides of dK / dV (and dQ)
+  int n, H, s, nq;
   float sl2, scale;
   int want_dq, want_dkdv;
   int* err;
@@ -341,6 +351,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   const int warp = warp_id(), lane = lane_id();
   const int jb = static_cast<int>(blockIdx.x) / p.n;  // key tile; jb = 0 has the most work
   const int head = static_cast<int>(blockIdx.x) % p.n;
+  const int bi = head / p.H, hi = head % p.H;
   const int n_it = p.nq - jb;
 
   if (smem_u32(smem) & 1023) {
@@ -377,14 +388,14 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       tma_prefetch_desc(&tmV);
       tma_prefetch_desc(&tmDO);
       mbar_expect_tx(kv_full, 2 * TILE);
-      tma_load_3d(&tmK, kv_full, smem + OFF_K, 0, jb * BKV, head);
-      tma_load_3d(&tmV, kv_full, smem + OFF_V, 0, jb * BKV, head);
+      tma_load_4d(&tmK, kv_full, smem + OFF_K, 0, jb * BKV, hi, bi);
+      tma_load_4d(&tmV, kv_full, smem + OFF_V, 0, jb * BKV, hi, bi);
       for (int it = 0; it < n_it; ++it) {
         const int slot = it & 1, i = jb + it;
         if (!mbar_wait(&qdo_empty[slot], ((it >> 1) & 1) ^ 1, ab)) break;
         mbar_expect_tx(&qdo_full[slot], 2 * TILE);
-        tma_load_3d(&tmQ, &qdo_full[slot], smem + OFF_Q + slot * TILE, 0, i * BQ, head);
-        tma_load_3d(&tmDO, &qdo_full[slot], smem + OFF_DO + slot * TILE, 0, i * BQ, head);
+        tma_load_4d(&tmQ, &qdo_full[slot], smem + OFF_Q + slot * TILE, 0, i * BQ, hi, bi);
+        tma_load_4d(&tmDO, &qdo_full[slot], smem + OFF_DO + slot * TILE, 0, i * BQ, hi, bi);
       }
     }
   } else if (warp == 1) {
@@ -510,7 +521,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       tc_fence_after();
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
-        __nv_bfloat16* dst = (which == 0 ? p.dV : p.dK) + ((long long)head * p.s + kv) * HD;
+        __nv_bfloat16* dst = (which == 0 ? p.dV : p.dK) + bi * p.gs.b + (long long)kv * p.gs.s + hi * p.gs.h;
         const float mul = (which == 0) ? 1.f : p.scale;
         const uint32_t col = (which == 0) ? COL_DV : COL_DK;
 #pragma unroll
@@ -571,14 +582,17 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
 // D[row] = sum_d dO[row,d] * O[row,d]; optionally zero the dQ accumulator row.
 // One warp per row (64 bf16 = 32 bf16x2).
 __global__ void bwd_preprocess_kernel(const __nv_bfloat16* __restrict__ O, const __nv_bfloat16* __restrict__ dO,
-                                      float* __restrict__ D, float* __restrict__ dQacc, long long rows) {
+                                      Strides os, int H, int s, float* __restrict__ D, float* __restrict__ dQacc,
+                                      long long rows) {
   const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   float acc = 0.f;
   if (O != nullptr) {
-    const __nv_bfloat162 o = reinterpret_cast<const __nv_bfloat162*>(O + row * HD)[lane];
-    const __nv_bfloat162 g = reinterpret_cast<const __nv_bfloat162*>(dO + row * HD)[lane];
+    const long long nh = row / s, q = row % s;
+    const long long off = (nh / H) * os.b + q * os.s + (nh % H) * os.h;
+    const __nv_bfloat162 o = reinterpret_cast<const __nv_bfloat162*>(O + off)[lane];
+    const __nv_bfloat162 g = reinterpret_cast<const __nv_bfloat162*>(dO + off)[lane];
     const float2 of = __bfloat1622float2(o), gf = __bfloat1622float2(g);
     acc = of.x * gf.x + of.y * gf.y;
 #pragma unroll
@@ -588,12 +602,16 @@ __global__ void bwd_preprocess_kernel(const __nv_bfloat16* __restrict__ O, const
   if (dQacc) reinterpret_cast<float2*>(dQacc + row * HD)[lane] = make_float2(0.f, 0.f);
 }
 
-__global__ void dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dQ, float scale,
-                                  long long n4) {
+__global__ void dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dQ, Strides gs, int H,
+                                  int s, float scale, long long n4) {
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n4) return;
+  const long long row = i >> 4, c4 = i & 15;
+  const long long nh = row / s, q = row % s;
+  const long long off = (nh / H) * gs.b + q * gs.s + (nh % H) * gs.h + c4 * 4;
   const float4 v = reinterpret_cast<const float4*>(acc)[i];
-  reinterpret_cast<uint2*>(dQ)[i] = make_uint2(pack_bf16x2(v.x * scale, v.y * scale), pack_bf16x2(v.z * scale, v.w * scale));
+  *reinterpret_cast<uint2*>(dQ + off) =
+      make_uint2(pack_bf16x2(v.x * scale, v.y * scale), pack_bf16x2(v.z * scale, v.w * scale));
 }
 
 static int check_common(const void* Q, const void* K, const void* V, int n, int s, int d) {
@@ -620,36 +638,44 @@ static int set_smem(Kern k, int bytes) {
 
 int* device_error_word();
 
-int flash_fwd(const void* Q, const void* K, const void* V, void* O, float* L, int n, int s, int d,
-              cudaStream_t stream) {
+// Strided forward: Q/K/V share strides qs, O uses os; L is contiguous [B*H, s].
+int flash_fwd(const void* Q, const void* K, const void* V, fa::Strides qs, void* O, fa::Strides os, float* L, int B,
+              int H, int s, int d, cudaStream_t stream) {
   using namespace fa;
-  int st = check_common(Q, K, V, n, s, d);
+  if (B <= 0 || H <= 0) return NL_ERR_SHAPE;
+  int st = check_common(Q, K, V, B * H, s, d);
   if (st) return st;
-  if (reinterpret_cast<uintptr_t>(O) & 15) return NL_ERR_ALIGN;
+  if ((reinterpret_cast<uintptr_t>(O) & 15) || (os.s & 7) || (os.h & 7) || (os.b & 7)) return NL_ERR_ALIGN;
   CUtensorMap tq, tk, tv;
-  if ((st = make_tmap_bf16_3d(&tq, Q, HD, s, n, 64, BQ))) return st;
-  if ((st = make_tmap_bf16_3d(&tk, K, HD, s, n, 64, BKV))) return st;
-  if ((st = make_tmap_bf16_3d(&tv, V, HD, s, n, 64, BKV))) return st;
+  if ((st = make_tmap_bf16_4d(&tq, Q, s, H, B, qs.s, qs.h, qs.b, BQ))) return st;
+  if ((st = make_tmap_bf16_4d(&tk, K, s, H, B, qs.s, qs.h, qs.b, BKV))) return st;
+  if ((st = make_tmap_bf16_4d(&tv, V, s, H, B, qs.s, qs.h, qs.b, BKV))) return st;
   FwdParams p{};
   p.O = reinterpret_cast<__nv_bfloat16*>(O);
+  p.os = os;
   p.L = L;
-  p.n = n;
+  p.n = B * H;
+  p.H = H;
   p.s = s;
   p.nq = (s + BQ - 1) / BQ;
   p.sl2 = (1.f / sqrtf(static_cast<float>(HD))) * kLog2e;
   p.err = device_error_word();
   if ((st = set_smem(flash_fwd_kernel, fwd::SMEM))) return st;
-  const long long grid = static_cast<long long>(n) * p.nq;
+  const long long grid = static_cast<long long>(p.n) * p.nq;
   if (grid > 0x7fffffffLL) return NL_ERR_SHAPE;
   flash_fwd_kernel<<<static_cast<unsigned>(grid), fwd::kThreads, fwd::SMEM, stream>>>(tq, tk, tv, p);
   return launch_status();
 }
 
-// Full backward.  D (f32 [n,s]) and dQacc (f32 [n,s,64]) are caller workspaces;
-// if O is non-null, D is computed here from O and dO, otherwise D is an input.
-int flash_bwd(const void* Q, const void* K, const void* V, const void* O, const void* dO, const float* L,
-              float* D, void* dQ, void* dK, void* dV, float* dQacc, int n, int s, int d, cudaStream_t stream) {
+// Strided backward.  Q/K/V and dQ/dK/dV share strides qs; O/dO use os.
+// D (f32 [B*H, s]) and dQacc (f32 [B*H, s, 64]) are caller workspaces; if O is
+// non-null, D is computed here from O and dO, otherwise D is an input.
+int flash_bwd(const void* Q, const void* K, const void* V, fa::Strides qs, const void* O, const void* dO,
+              fa::Strides os, const float* L, float* D, void* dQ, void* dK, void* dV, float* dQacc, int B, int H, int s,
+              int d, cudaStream_t stream) {
   using namespace fa;
+  if (B <= 0 || H <= 0) return NL_ERR_SHAPE;
+  const int n = B * H;
   int st = check_common(Q, K, V, n, s, d);
   if (st) return st;
   if (!dO || !L || !D) return NL_ERR_SHAPE;
@@ -663,22 +689,24 @@ int flash_bwd(const void* Q, const void* K, const void* V, const void* O, const 
   if (O || want_dq) {
     const long long threads = rows * 32;
     bwd_preprocess_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
-        reinterpret_cast<const __nv_bfloat16*>(O), reinterpret_cast<const __nv_bfloat16*>(dO), D,
+        reinterpret_cast<const __nv_bfloat16*>(O), reinterpret_cast<const __nv_bfloat16*>(dO), os, H, s, D,
         want_dq ? dQacc : nullptr, rows);
     if ((st = launch_status())) return st;
   }
   CUtensorMap tq, tk, tv, tdo;
-  if ((st = make_tmap_bf16_3d(&tq, Q, HD, s, n, 64, BQ))) return st;
-  if ((st = make_tmap_bf16_3d(&tk, K, HD, s, n, 64, BKV))) return st;
-  if ((st = make_tmap_bf16_3d(&tv, V, HD, s, n, 64, BKV))) return st;
-  if ((st = make_tmap_bf16_3d(&tdo, dO, HD, s, n, 64, BQ))) return st;
+  if ((st = make_tmap_bf16_4d(&tq, Q, s, H, B, qs.s, qs.h, qs.b, BQ))) return st;
+  if ((st = make_tmap_bf16_4d(&tk, K, s, H, B, qs.s, qs.h, qs.b, BKV))) return st;
+  if ((st = make_tmap_bf16_4d(&tv, V, s, H, B, qs.s, qs.h, qs.b, BKV))) return st;
+  if ((st = make_tmap_bf16_4d(&tdo, dO, s, H, B, os.s, os.h, os.b, BQ))) return st;
   BwdParams p{};
   p.L = L;
   p.D = D;
   p.dQacc = dQacc;
   p.dK = reinterpret_cast<__nv_bfloat16*>(dK);
   p.dV = reinterpret_cast<__nv_bfloat16*>(dV);
+  p.gs = qs;
   p.n = n;
+  p.H = H;
   p.s = s;
   p.nq = (s + BQ - 1) / BQ;
   p.scale = 1.f / sqrtf(static_cast<float>(HD));
@@ -693,7 +721,7 @@ int flash_bwd(const void* Q, const void* K, const void* V, const void* O, const 
   if (want_dq) {
     const long long n4 = rows * HD / 4;
     dq_convert_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, stream>>>(
-        dQacc, reinterpret_cast<__nv_bfloat16*>(dQ), p.scale, n4);
+        dQacc, reinterpret_cast<__nv_bfloat16*>(dQ), qs, H, s, p.scale, n4);
     if ((st = launch_status())) return st;
   }
   return NL_OK;
@@ -701,29 +729,54 @@ int flash_bwd(const void* Q, const void* K, const void* V, const void* O, const 
 
 }  // namespace nl
 
+namespace {
+// Contiguous [n, s, 64] as the strided form with B = n, H = 1.
+inline nl::fa::Strides contiguous(int s) { return nl::fa::Strides{64, 64LL * s, 64LL * s}; }
+}  // namespace
+
 extern "C" int nl_flash_attention_fwd(const void* Q, const void* K, const void* V, void* O, float* L, int n, int s,
                                       int d, cudaStream_t stream) {
-  return nl::flash_fwd(Q, K, V, O, L, n, s, d, stream);
+  return nl::flash_fwd(Q, K, V, contiguous(s), O, contiguous(s), L, n, 1, s, d, stream);
 }
 
 extern "C" int nl_flash_attention_bwd(const void* Q, const void* K, const void* V, const void* O, const void* dO,
                                       const float* L, float* D_ws, void* dQ, void* dK, void* dV, float* dQacc_ws,
                                       int n, int s, int d, cudaStream_t stream) {
   if (!O) return NL_ERR_SHAPE;
-  return nl::flash_bwd(Q, K, V, O, dO, L, D_ws, dQ, dK, dV, dQacc_ws, n, s, d, stream);
+  return nl::flash_bwd(Q, K, V, contiguous(s), O, dO, contiguous(s), L, D_ws, dQ, dK, dV, dQacc_ws, n, 1, s, d,
+                       stream);
 }
 
 extern "C" int nl_flash_attention_bwd_dq(const void* Q, const void* K, const void* V, const void* dO,
                                          const float* L, const float* D, void* dQ, float* dQacc_ws, int n, int s,
                                          int d, cudaStream_t stream) {
   if (!dQ) return NL_ERR_SHAPE;
-  return nl::flash_bwd(Q, K, V, nullptr, dO, L, const_cast<float*>(D), dQ, nullptr, nullptr, dQacc_ws, n, s, d,
-                       stream);
+  return nl::flash_bwd(Q, K, V, contiguous(s), nullptr, dO, contiguous(s), L, const_cast<float*>(D), dQ, nullptr,
+                       nullptr, dQacc_ws, n, 1, s, d, stream);
 }
 
 extern "C" int nl_flash_attention_bwd_dkdv(const void* Q, const void* K, const void* V, const void* dO,
                                            const float* L, const float* D, void* dK, void* dV, int n, int s, int d,
                                            cudaStream_t stream) {
   if (!dK || !dV) return NL_ERR_SHAPE;
-  return nl::flash_bwd(Q, K, V, nullptr, dO, L, const_cast<float*>(D), nullptr, dK, dV, nullptr, n, s, d, stream);
+  return nl::flash_bwd(Q, K, V, contiguous(s), nullptr, dO, contiguous(s), L, const_cast<float*>(D), nullptr, dK,
+                       dV, nullptr, n, 1, s, d, stream);
+}
+
+extern "C" int nl_flash_attention_fwd_strided(const void* Q, const void* K, const void* V, long long q_s,
+                                              long long q_h, long long q_b, void* O, long long o_s, long long o_h,
+                                              long long o_b, float* L, int B, int H, int s, int d,
+                                              cudaStream_t stream) {
+  return nl::flash_fwd(Q, K, V, nl::fa::Strides{q_s, q_h, q_b}, O, nl::fa::Strides{o_s, o_h, o_b}, L, B, H, s, d,
+                       stream);
+}
+
+extern "C" int nl_flash_attention_bwd_strided(const void* Q, const void* K, const void* V, long long q_s,
+                                              long long q_h, long long q_b, const void* O, const void* dO,
+                                              long long o_s, long long o_h, long long o_b, const float* L,
+                                              float* D_ws, void* dQ, void* dK, void* dV, float* dQacc_ws, int B,
+                                              int H, int s, int d, cudaStream_t stream) {
+  if (!O) return NL_ERR_SHAPE;
+  return nl::flash_bwd(Q, K, V, nl::fa::Strides{q_s, q_h, q_b}, O, dO, nl::fa::Strides{o_s, o_h, o_b}, L, D_ws, dQ,
+                       dK, dV, dQacc_ws, B, H, s, d, stream);
 }

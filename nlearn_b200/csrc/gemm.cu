@@ -17,6 +17,7 @@
 // few-tile dW GEMMs) accumulates with vector float atomics.
 #include "sm100.cuh"
 #include "host_common.h"
+#include "gemm.h"
 
 namespace nl {
 namespace gemm {
@@ -24,7 +25,6 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle row of bf16
 constexpr int kThreads = 6 * 32;
-constexpr int kEpiWarp0 = 2;
 
 struct Params {
   int M, N, K;
@@ -38,6 +38,15 @@ struct Params {
   __nv_bfloat16* aux;
   const void* resid;
   int* err;
+  // fused LM-head cross-entropy epilogues
+  const int* targets;   // [M] target column (global vocab index)
+  float2* part;         // LCE_STATS: [tiles_n, M] per-tile (max, sum 2^(y-max)), base-2 units
+  float* tgt_logit;     // LCE_STATS: [M] logit of the target column
+  const float* lse;     // LCE_GRAD: [M] natural-log logsumexp
+  const float* gptr;    // LCE_GRAD: optional device scalar multiplying grad_scale
+  float grad_scale;     // LCE_GRAD: dlogits multiplier (1/M for a mean loss)
+  int v_valid;          // columns >= v_valid are vocabulary padding (masked)
+  int col_offset;       // global vocab index of this launch's column 0
 };
 
 template <int BN>
@@ -71,6 +80,58 @@ __device__ __forceinline__ void decode_unit(const Params& p, int u, int& mb, int
   const int r = t - g * per_group;
   mb = first_m + r % gsz;
   nb = r / gsz;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Online (max, sum-exp) of 32 logits of one row, base 2; padding columns masked.
+__device__ __forceinline__ void lce_stats_chunk(const Params& p, int row, int col0, const float (&v)[32], float& m,
+                                                float& s, float& tl, int t) {
+  float y[32];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    y[i] = (col0 + i < p.v_valid) ? v[i] * kLog2e : -INFINITY;
+    mx = fmaxf(mx, y[i]);
+    if (col0 + i == t) tl = v[i];
+  }
+  if (mx == -INFINITY) return;
+  if (mx > m) {
+    s *= ex2_approx(m - mx);
+    m = mx;
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) s += ex2_approx(y[i] - m);
+}
+
+// dlogits = (softmax - onehot) * scale for 32 columns, bf16 out; padding -> 0.
+__device__ __forceinline__ void lce_grad_chunk(const Params& p, int row, int col0, const float (&v)[32], float lse2,
+                                               int t, float scale) {
+  if (row >= p.M) return;
+  uint32_t pk[16];
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    float d[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = col0 + i + h;
+      const float pr = ex2_approx(v[i + h] * kLog2e - lse2);
+      d[h] = (c < p.v_valid) ? (pr - (c == t ? 1.f : 0.f)) * scale : 0.f;
+    }
+    pk[i / 2] = pack_bf16x2(d[0], d[1]);
+  }
+  __nv_bfloat16* cb = reinterpret_cast<__nv_bfloat16*>(p.C) + (long long)row * p.ldc + col0;
+  if (col0 + 32 <= p.N && (p.ldc & 7) == 0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      reinterpret_cast<uint4*>(cb)[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+  } else {
+    for (int i = 0; i < 32 && col0 + i < p.N; ++i) {
+      const uint32_t w = pk[i / 2];
+      const unsigned short h = (i & 1) ? (w >> 16) : (w & 0xffff);
+      cb[i] = __ushort_as_bfloat16(h);
+    }
+  }
 }
 
 // Epilogue for one thread: row `row`, 32 consecutive columns from `col0`.
@@ -300,6 +361,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row = mb * BM + q * 32 + lane;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      const bool lce = p.epi >= NL_EPI_LCE_STATS;
+      int t = -1;
+      float lse2 = 0.f, gsc = 0.f, m = -INFINITY, ssum = 0.f, tl = 0.f;
+      if (lce && row < p.M) {
+        t = p.targets[row] - p.col_offset;
+        if (p.epi == NL_EPI_LCE_GRAD) {
+          lse2 = p.lse[row] * kLog2e;
+          gsc = p.grad_scale * (p.gptr ? *p.gptr : 1.f);
+        }
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         const int col0 = nb * BN + c * 32;
@@ -310,7 +381,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        epi_chunk(p, row, col0, v);
+        if (!lce) epi_chunk(p, row, col0, v);
+        else if (p.epi == NL_EPI_LCE_STATS) lce_stats_chunk(p, row, col0, v, m, ssum, tl, t);
+        else lce_grad_chunk(p, row, col0, v, lse2, t, gsc);
+      }
+      if (p.epi == NL_EPI_LCE_STATS && row < p.M) {
+        p.part[(long long)nb * p.M + row] = make_float2(m, ssum);
+        if (t >= nb * BN && t < nb * BN + BN && t < p.N) p.tgt_logit[row] = tl;
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
@@ -351,13 +428,16 @@ int* device_error_word();
 
 int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long ldb, int b_trans, void* Cp,
              long long ldc, int c_dtype, int M, int N, int K, float alpha, int epi, const float* bias, void* aux,
-             const void* resid, cudaStream_t stream) {
+             const void* resid, cudaStream_t stream, const GemmExtra* ex) {
   using namespace gemm;
   if (M <= 0 || N <= 0 || K < 0) return NL_ERR_SHAPE;
   if (c_dtype != NL_F32 && c_dtype != NL_BF16) return NL_ERR_DTYPE;
-  if (epi < NL_EPI_STORE || epi > NL_EPI_RESID) return NL_ERR_SHAPE;
+  if (epi < NL_EPI_STORE || epi > NL_EPI_LCE_GRAD) return NL_ERR_SHAPE;
   if (epi == NL_EPI_ACCUM && c_dtype != NL_F32) return NL_ERR_DTYPE;
   if (epi == NL_EPI_BIAS_GELU && (c_dtype != NL_BF16 || aux == nullptr)) return NL_ERR_DTYPE;
+  if (epi >= NL_EPI_LCE_STATS && (ex == nullptr || ex->targets == nullptr)) return NL_ERR_WORKSPACE;
+  if (epi == NL_EPI_LCE_STATS && (ex->part == nullptr || ex->tgt_logit == nullptr)) return NL_ERR_WORKSPACE;
+  if (epi == NL_EPI_LCE_GRAD && (ex->lse == nullptr || c_dtype != NL_BF16)) return NL_ERR_WORKSPACE;
   if (K == 0) {
     if (epi == NL_EPI_ACCUM) return NL_OK;
     return NL_ERR_SHAPE;
@@ -376,6 +456,16 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
   p.resid = resid;
   p.err = device_error_word();
   p.num_kb = (K + BK - 1) / BK;
+  if (ex) {
+    p.targets = ex->targets;
+    p.part = ex->part;
+    p.tgt_logit = ex->tgt_logit;
+    p.lse = ex->lse;
+    p.gptr = ex->gptr;
+    p.grad_scale = ex->grad_scale;
+    p.v_valid = ex->v_valid;
+    p.col_offset = ex->col_offset;
+  }
 
   const bool a_mn = a_trans != 0;
   const bool b_mn = b_trans == 0;
@@ -385,6 +475,7 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
   {
     const long long t256 = (long long)((M + BM - 1) / BM) * ((N + 255) / 256);
     if (N <= 128 || t256 < sms) BN = 128;
+    if (ex && ex->force_bn) BN = ex->force_bn;
   }
   p.tiles_m = (M + BM - 1) / BM;
   p.tiles_n = (N + BN - 1) / BN;
@@ -426,11 +517,12 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
 extern "C" int nl_gemm_ex(const void* A, int lda, int a_trans, const void* B, int ldb, int b_trans, void* C,
                           int ldc, int c_dtype, int M, int N, int K, float alpha, int epilogue, const float* bias,
                           void* aux, const void* resid, cudaStream_t stream) {
+  if (epilogue > NL_EPI_RESID) return NL_ERR_SHAPE;  // LCE epilogues go through nl_lce_*
   return nl::gemm_run(A, lda, a_trans, B, ldb, b_trans, C, ldc, c_dtype, M, N, K, alpha, epilogue, bias, aux,
-                      resid, stream);
+                      resid, stream, nullptr);
 }
 
 extern "C" int nl_gemm(const void* A, const void* B, float* C, int M, int N, int K, cudaStream_t stream) {
   return nl::gemm_run(A, K, 0, B, N, 0, C, N, NL_F32, M, N, K, 1.0f, NL_EPI_STORE, nullptr, nullptr, nullptr,
-                      stream);
+                      stream, nullptr);
 }

@@ -58,6 +58,27 @@ inline int make_tmap_bf16_3d(CUtensorMap* m, const void* base, uint64_t cols, ui
   return r == CUDA_SUCCESS ? NL_OK : NL_ERR_CUDA;
 }
 
+// Strided 4-D bf16 tensor [b][h][s][64 cols] addressed with element strides
+// (s_stride, h_stride, b_stride), boxes of 64 x box_rows x 1 x 1, SW128.
+// Covers both contiguous [n, s, 64] (h = 1) and head-interleaved activations
+// such as a fused QKV projection [b, s, 3, H, 64].
+inline int make_tmap_bf16_4d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t heads, uint64_t batch,
+                             uint64_t s_stride, uint64_t h_stride, uint64_t b_stride, uint32_t box_rows) {
+  auto fn = encode_tiled_fn();
+  if (!fn) return NL_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((s_stride * 2) & 15) || ((h_stride * 2) & 15) ||
+      ((b_stride * 2) & 15))
+    return NL_ERR_ALIGN;
+  cuuint64_t dims[4] = {64, rows, heads, batch};
+  cuuint64_t strides[3] = {s_stride * 2, h_stride * 2, b_stride * 2};
+  cuuint32_t box[4] = {64, box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NL_OK : NL_ERR_CUDA;
+}
+
 inline int sm_count() {
   int dev = 0, n = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);

@@ -14,6 +14,8 @@ into bf16 dlogits for the dX / dW GEMMs, one vocabulary chunk at a time.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from .._lib import BF16, F32, check, lib, ptr, stream_handle
@@ -95,4 +97,80 @@ def cross_entropy(logits: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
     return _CE.apply(logits.reshape(-1, V), targets.reshape(-1))
 
 
-__all__ = ["cross_entropy", "_ce_fwd_raw", "_ce_bwd_raw", "ce_fwd_bwd"]
+# Vocabulary chunk of the fused backward (the reference's NLEARN_LCE_CHUNK,
+# cross_entropy.py:91); rounded to a multiple of 64 columns.
+_LCE_CHUNK = max(64, int(os.environ.get("NLEARN_LCE_CHUNK", "8192")) // 64 * 64)
+
+
+def _lce_operands(X, W):
+    Xb = X.to(torch.bfloat16)
+    if Xb.stride(-1) != 1 or Xb.stride(0) % 8 or Xb.data_ptr() % 16:
+        Xb = Xb.contiguous()
+    Wb = W.to(torch.bfloat16)
+    D, V = Wb.shape
+    if Wb.stride(-1) != 1 or Wb.stride(0) % 8 or Wb.data_ptr() % 16:
+        Vp = (V + 7) // 8 * 8
+        Wp = torch.zeros(D, Vp, device=Wb.device, dtype=torch.bfloat16)
+        Wp[:, :V] = Wb
+        Wb = Wp[:, :V]
+    return Xb, Wb
+
+
+def lce_fwd_raw(Xb, Wb, t):
+    """-> loss[M], lse[M] (f32) through nl_lce_fwd."""
+    M, D = Xb.shape
+    V = Wb.shape[1]
+    loss = torch.empty(M, device=Xb.device, dtype=torch.float32)
+    lse = torch.empty(M, device=Xb.device, dtype=torch.float32)
+    nbytes = lib.nl_lce_workspace_bytes(M, V, 0)
+    ws = torch.empty(nbytes, device=Xb.device, dtype=torch.uint8)
+    check(lib.nl_lce_fwd(ptr(Xb), Xb.stride(0), ptr(Wb), Wb.stride(0), ptr(t), ptr(loss), ptr(lse), ptr(ws), nbytes,
+                         M, D, V, stream_handle()), "nl_lce_fwd")
+    return loss, lse
+
+
+def lce_bwd_raw(Xb, Wb, t, lse, g=None, dX=None, dW=None, dw_accumulate=False, chunk=None):
+    """-> dX f32 [M,D] (accumulated into `dX` if given), dW f32 [D,V] (row pitch of W)."""
+    M, D = Xb.shape
+    V = Wb.shape[1]
+    chunk = chunk or _LCE_CHUNK
+    if dX is None:
+        dX = torch.zeros(M, D, device=Xb.device, dtype=torch.float32)
+    if dW is None:
+        dW = torch.empty(D, Wb.stride(0), device=Xb.device, dtype=torch.float32)[:, :V]
+    gp = None if g is None else g.detach().float().reshape(1).contiguous()
+    nbytes = lib.nl_lce_workspace_bytes(M, V, chunk)
+    ws = torch.empty(nbytes, device=Xb.device, dtype=torch.uint8)
+    check(lib.nl_lce_bwd(ptr(Xb), Xb.stride(0), ptr(Wb), Wb.stride(0), ptr(t), ptr(lse), ptr(gp), 1.0 / M, ptr(dX),
+                         ptr(dW), dW.stride(0), int(dw_accumulate), ptr(ws), nbytes, chunk, M, D, V,
+                         stream_handle()), "nl_lce_bwd")
+    return dX, dW
+
+
+class _LCE(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, X, W, targets):
+        Xb, Wb = _lce_operands(X, W)
+        t = targets.reshape(-1).to(torch.int32).contiguous()
+        loss, lse = lce_fwd_raw(Xb, Wb, t)
+        ctx.save_for_backward(Xb, Wb, t, lse)
+        ctx.dtypes = (X.dtype, W.dtype)
+        return loss.mean()
+
+    @staticmethod
+    def backward(ctx, g):
+        Xb, Wb, t, lse = ctx.saved_tensors
+        dX, dW = lce_bwd_raw(Xb, Wb, t, lse, g=g)
+        return dX.to(ctx.dtypes[0]), dW.to(ctx.dtypes[1]), None
+
+
+def linear_cross_entropy(X: torch.Tensor, W: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+    """Mean softmax CE of logits = X[M,D] @ W[D,V] against targets[M], without
+    materialising the (M, V) logits (reference cross_entropy.py:131-136)."""
+    if not X.is_cuda:
+        raise ValueError("nlearn_b200 linear_cross_entropy runs on CUDA tensors only (no CPU fallback)")
+    return _LCE.apply(X, W, targets)
+
+
+__all__ = ["cross_entropy", "linear_cross_entropy", "_ce_fwd_raw", "_ce_bwd_raw", "ce_fwd_bwd", "lce_fwd_raw",
+           "lce_bwd_raw"]

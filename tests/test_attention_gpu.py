@@ -120,3 +120,34 @@ def test_deterministic_forward(cuda):
     O1, L1 = A._flash_fwd_raw(Q, K, V)
     O2, L2 = A._flash_fwd_raw(Q, K, V)
     assert torch.equal(O1, O2) and torch.equal(L1, L2)
+
+
+def test_strided_qkv_layout(cuda):
+    # Q/K/V read in place from a fused projection [B, S, 3, H, 64]; O written
+    # as [B, S, H, 64]; dQ/dK/dV written back into the [B, S, 3, H, 64] layout.
+    from nlearn_b200._lib import lib, ptr, stream_handle, check
+    B, S, H = 3, 384, 4
+    torch.manual_seed(3)
+    qkv = torch.randn(B, S, 3, H, 64, device=cuda).bfloat16()
+    dO = torch.randn(B, S, H, 64, device=cuda).bfloat16()
+    O = torch.empty(B, S, H, 64, device=cuda, dtype=torch.bfloat16)
+    L = torch.empty(B * H, S, device=cuda)
+    qs = (3 * H * 64, 64, S * 3 * H * 64)
+    os_ = (H * 64, 64, S * H * 64)
+    check(lib.nl_flash_attention_fwd_strided(ptr(qkv[:, :, 0]), ptr(qkv[:, :, 1]), ptr(qkv[:, :, 2]), *qs, ptr(O),
+                                             *os_, ptr(L), B, H, S, 64, stream_handle()), "fwd_strided")
+    dqkv = torch.empty_like(qkv)
+    D = torch.empty(B * H, S, device=cuda)
+    acc = torch.empty(B * H, S, 64, device=cuda)
+    check(lib.nl_flash_attention_bwd_strided(ptr(qkv[:, :, 0]), ptr(qkv[:, :, 1]), ptr(qkv[:, :, 2]), *qs, ptr(O),
+                                             ptr(dO), *os_, ptr(L), ptr(D), ptr(dqkv[:, :, 0]), ptr(dqkv[:, :, 1]),
+                                             ptr(dqkv[:, :, 2]), ptr(acc), B, H, S, 64, stream_handle()),
+          "bwd_strided")
+    to_c = lambda x: x.permute(0, 2, 1, 3).reshape(B * H, S, 64).contiguous()
+    Qc, Kc, Vc = (to_c(qkv[:, :, i]) for i in range(3))
+    Oc, Lc = A._flash_fwd_raw(Qc, Kc, Vc)
+    dQc, dKc, dVc = A._flash_bwd_raw(Qc, Kc, Vc, Oc, Lc, to_c(dO))
+    torch.cuda.synchronize()
+    assert torch.equal(to_c(O), Oc) and torch.equal(L, Lc)
+    assert torch.equal(to_c(dqkv[:, :, 1]), dKc) and torch.equal(to_c(dqkv[:, :, 2]), dVc)
+    assert ((to_c(dqkv[:, :, 0]).float() - dQc.float()).abs().max() <= 1e-2 * dQc.float().abs().max())
