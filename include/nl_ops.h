@@ -51,8 +51,9 @@ typedef enum {
   NL_EPI_BIAS = 2,      /* C = alpha*A.B + bias[N]       (bias f32)            */
   NL_EPI_BIAS_GELU = 3, /* aux = A.B + bias; C = gelu_tanh(aux)  (C, aux bf16) */
   NL_EPI_RESID = 4,     /* C = alpha*A.B + bias? + resid (resid in c_dtype)    */
-  NL_EPI_LCE_STATS = 5, /* internal: fused LM-head CE partial row statistics   */
-  NL_EPI_LCE_GRAD = 6   /* internal: fused LM-head CE dlogits (bf16)           */
+  NL_EPI_DGELU = 5,     /* C = (alpha*A.B) * gelu_tanh'(aux)   (C, aux bf16)   */
+  NL_EPI_LCE_STATS = 6, /* internal: fused LM-head CE partial row statistics   */
+  NL_EPI_LCE_GRAD = 7   /* internal: fused LM-head CE dlogits (bf16)           */
 } nl_epilogue;
 
 /* Library / device introspection. */
@@ -60,6 +61,8 @@ NL_API const char* nl_version(void);
 /* Reads and clears the device-side error word (1 = a bounded wait timed out).
  * Synchronises `stream`. */
 NL_API int nl_get_device_error(cudaStream_t stream);
+/* Kernels launched by this library so far in this process (host-side count). */
+NL_API long long nl_launch_count(void);
 
 /* ---------------------------------------------------------------- GEMM
  * Replaces target `gemm` (nlearn/kernels/gemm.py:32-40 `_gemm_raw`;
@@ -144,6 +147,33 @@ NL_API int nl_flash_attention_bwd_strided(const void* Q, const void* K, const vo
                                           long long q_b, const void* O, const void* dO, long long o_s, long long o_h,
                                           long long o_b, const float* L, float* D_ws, void* dQ, void* dK, void* dV,
                                           float* dQacc_ws, int B, int H, int s, int d, cudaStream_t stream);
+
+/* ---------------------------------------------------------------- training-step tail
+ * Memory-bound kernels around the hot path (no reference custom-call: nlearn
+ * leaves these to XLA, nlearn/model.py:74-90, 228-241 and train.py:338-339).
+ * Activations bf16 row-major [M, D] (D % 256 == 0), statistics / grads f32. */
+/* x[m] = wte[tok[m]] + wpe[m % S] (bf16 tables). */
+NL_API int nl_embed_fwd(const int* tok, const void* wte, const void* wpe, void* out, int M, int S, int D,
+                        cudaStream_t stream);
+/* dwte[tok[m]] += dx[m], dwpe[m % S] += dx[m] (f32, atomics). */
+NL_API int nl_embed_bwd(const int* tok, const float* dx, float* dwte, float* dwpe, int M, int S, int D,
+                        cudaStream_t stream);
+/* y = LayerNorm(x; g, b, eps); saves per-row mean, rstd. */
+NL_API int nl_layernorm_fwd(const void* x, const float* g, const float* b, void* y, float* mean, float* rstd, int M,
+                            int D, float eps, cudaStream_t stream);
+/* dres (f32) = (accumulate ? dres : 0) + dLN/dx . dy; dres_bf16 = bf16(dres);
+ * dg += sum dy*xhat, db += sum dy. */
+NL_API int nl_layernorm_bwd(const void* dy, const void* x, const float* mean, const float* rstd, const float* g,
+                            float* dres, void* dres_bf16, float* dg, float* db, int M, int D, int accumulate,
+                            cudaStream_t stream);
+/* out[N] += column sums of bf16 x[M, N] (N % 8 == 0). */
+NL_API int nl_colsum_bf16(const void* x, float* out, int M, int N, cudaStream_t stream);
+/* AdamW on a flat f32 buffer (optax.adamw semantics); hyper = device
+ * f32[3] {lr, 1-b1^t, 1-b2^t}; also writes the bf16 compute copy if non-NULL.
+ * n % 4 == 0. */
+NL_API int nl_adamw_step(float* p, const float* g, float* m, float* v, void* shadow_bf16, long long n,
+                         const float* hyper, float b1, float b2, float eps, float wd, cudaStream_t stream);
+NL_API int nl_cast_bf16(const float* x, void* y, long long n, cudaStream_t stream);
 
 /* ---------------------------------------------------------------- fused LM-head CE
  * Replaces the jnp-chunked `linear_cross_entropy` (nlearn/kernels/

@@ -20,12 +20,13 @@ LIB_PATH = Path(__file__).resolve().with_name("libnl_ops.so")
 STATUS = {0: "NL_OK", -1: "NL_ERR_SHAPE", -2: "NL_ERR_ALIGN", -3: "NL_ERR_LAUNCH", -4: "NL_ERR_CUDA",
           -5: "NL_ERR_DTYPE", -6: "NL_ERR_WORKSPACE"}
 F32, BF16 = 0, 1
-EPI_STORE, EPI_ACCUM, EPI_BIAS, EPI_BIAS_GELU, EPI_RESID = 0, 1, 2, 3, 4
+EPI_STORE, EPI_ACCUM, EPI_BIAS, EPI_BIAS_GELU, EPI_RESID, EPI_DGELU = 0, 1, 2, 3, 4, 5
 
 # name -> argtypes (restype is int unless listed in _RESTYPE)
 SIGNATURES: dict[str, list] = {
     "nl_version": [],
     "nl_get_device_error": [c_void_p],
+    "nl_launch_count": [],
     "nl_gemm": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
     "nl_gemm_ex": [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int,
                    c_float, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
@@ -42,13 +43,20 @@ SIGNATURES: dict[str, list] = {
                                       [c_void_p, c_int, c_int, c_int, c_int, c_void_p],
     "nl_flash_attention_bwd_strided": [c_void_p] * 3 + [c_longlong] * 3 + [c_void_p] * 2 + [c_longlong] * 3 +
                                       [c_void_p] * 6 + [c_int, c_int, c_int, c_int, c_void_p],
+    "nl_embed_fwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
+    "nl_embed_bwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
+    "nl_layernorm_fwd": [c_void_p] * 6 + [c_int, c_int, c_float, c_void_p],
+    "nl_layernorm_bwd": [c_void_p] * 9 + [c_int, c_int, c_int, c_void_p],
+    "nl_colsum_bf16": [c_void_p, c_void_p, c_int, c_int, c_void_p],
+    "nl_adamw_step": [c_void_p] * 5 + [c_longlong, c_void_p, c_float, c_float, c_float, c_float, c_void_p],
+    "nl_cast_bf16": [c_void_p, c_void_p, c_longlong, c_void_p],
     "nl_lce_workspace_bytes": [c_int, c_int, c_int],
     "nl_lce_fwd": [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t,
                    c_int, c_int, c_int, c_void_p],
     "nl_lce_bwd": [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
                    c_int, c_int, c_void_p, ctypes.c_size_t, c_int, c_int, c_int, c_int, c_void_p],
 }
-_RESTYPE = {"nl_version": ctypes.c_char_p, "nl_lce_workspace_bytes": ctypes.c_size_t}
+_RESTYPE = {"nl_version": ctypes.c_char_p, "nl_launch_count": c_longlong, "nl_lce_workspace_bytes": ctypes.c_size_t}
 
 
 class NlError(RuntimeError):
@@ -101,4 +109,5 @@ def device_error() -> int:
 
 
 __all__ = ["lib", "check", "ptr", "stream_handle", "device_error", "NlError", "LIB_PATH", "SIGNATURES",
-           "F32", "BF16", "EPI_STORE", "EPI_ACCUM", "EPI_BIAS", "EPI_BIAS_GELU", "EPI_RESID", "c_longlong"]
+           "F32", "BF16", "EPI_STORE", "EPI_ACCUM", "EPI_BIAS", "EPI_BIAS_GELU", "EPI_RESID", "EPI_DGELU",
+           "c_longlong"]

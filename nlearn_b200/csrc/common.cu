@@ -1,5 +1,7 @@
 // common.cu — library-wide state: the device error word that bounded waits
 // write on timeout, and version / error introspection entry points.
+#include <atomic>
+
 #include <cuda_runtime.h>
 
 #include "host_common.h"
@@ -22,7 +24,12 @@ int* device_error_word() {
   return cached[dev];
 }
 
+static std::atomic<long long> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 }  // namespace nl
+
+extern "C" long long nl_launch_count(void) { return nl::g_launches.load(std::memory_order_relaxed); }
 
 extern "C" const char* nl_version(void) { return "nlearn-b200 0.1 (sm_100a)"; }
 

@@ -1,0 +1,372 @@
+// elementwise.cu — the memory-bound tail around the hot GEMM / attention / CE
+// kernels in the training step: token+position embedding, LayerNorm forward /
+// backward, bias-gradient column sums, and the fused AdamW update that also
+// refreshes the bf16 compute copy of the weights.
+//
+// Reference semantics: embeddings nlearn/model.py:74-90 (token + learned
+// position table of the BASELINE model), pre-LN LayerNorm with gamma/beta and
+// eps 1e-5 (the BASELINE model; iree_metal/kernels/test/bf16_metal_test.py:6-12),
+// AdamW as optax.adamw (nlearn/train.py:503-508: b1 0.9, b2 0.999, eps 1e-8,
+// decoupled weight decay on every leaf).
+//
+// All kernels are bandwidth-bound row/element kernels: 16-byte vector access,
+// one warp per row for the row reductions, grid-stride loops sized to the SMs.
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include "host_common.h"
+#include "sm100.cuh"
+
+namespace nl {
+namespace ew {
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 v = __bfloat1622float2(h[i]);
+    f[2 * i] = v.x;
+    f[2 * i + 1] = v.y;
+  }
+}
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                    pack_bf16x2(f[6], f[7]));
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// x[m, :] = wte[tok[m], :] + wpe[m % S, :]   (bf16 tables, bf16 out)
+template <int DV>  // D / 256: vectors of 8 per lane
+__global__ void embed_fwd_kernel(const int* __restrict__ tok, const __nv_bfloat16* __restrict__ wte,
+                                 const __nv_bfloat16* __restrict__ wpe, __nv_bfloat16* __restrict__ out, int M,
+                                 int S, int D) {
+  const int lane = threadIdx.x & 31;
+  for (long long m = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; m < M;
+       m += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
+    const int t = tok[m];
+    const uint4* a = reinterpret_cast<const uint4*>(wte + static_cast<long long>(t) * D);
+    const uint4* b = reinterpret_cast<const uint4*>(wpe + static_cast<long long>(m % S) * D);
+    uint4* o = reinterpret_cast<uint4*>(out + m * D);
+#pragma unroll
+    for (int j = 0; j < DV; ++j) {
+      float fa[8], fb[8];
+      unpack8(a[lane + 32 * j], fa);
+      unpack8(b[lane + 32 * j], fb);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) fa[i] += fb[i];
+      o[lane + 32 * j] = pack8(fa);
+    }
+  }
+}
+
+// dwte[tok[m]] += dx[m]; dwpe[m % S] += dx[m]   (f32 gradients, float atomics)
+template <int DV>
+__global__ void embed_bwd_kernel(const int* __restrict__ tok, const float* __restrict__ dx, float* dwte,
+                                 float* dwpe, int M, int S, int D) {
+  const int lane = threadIdx.x & 31;
+  for (long long m = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; m < M;
+       m += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
+    const int t = tok[m];
+    const float4* g = reinterpret_cast<const float4*>(dx + m * D);
+    float4* a = reinterpret_cast<float4*>(dwte + static_cast<long long>(t) * D);
+    float4* b = reinterpret_cast<float4*>(dwpe + static_cast<long long>(m % S) * D);
+#pragma unroll
+    for (int j = 0; j < 2 * DV; ++j) {
+      const float4 v = g[lane + 32 * j];
+      atomicAdd(a + lane + 32 * j, v);
+      atomicAdd(b + lane + 32 * j, v);
+    }
+  }
+}
+
+// y = (x - mean) * rstd * g + b;  per-row mean / rstd saved for the backward.
+template <int DV>
+__global__ void layernorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ g,
+                                     const float* __restrict__ b, __nv_bfloat16* __restrict__ y,
+                                     float* __restrict__ mean_out, float* __restrict__ rstd_out, int M, int D,
+                                     float eps) {
+  const int lane = threadIdx.x & 31;
+  for (long long m = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; m < M;
+       m += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + m * D);
+    float v[DV][8];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < DV; ++j) {
+      unpack8(xr[lane + 32 * j], v[j]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += v[j][i];
+    }
+    const float mean = warp_sum(s) / D;
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < DV; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = v[j][i] - mean;
+        q += d * d;
+      }
+    const float rstd = rsqrtf(warp_sum(q) / D + eps);
+    uint4* yr = reinterpret_cast<uint4*>(y + m * D);
+#pragma unroll
+    for (int j = 0; j < DV; ++j) {
+      const int c = (lane + 32 * j) * 8;
+      float o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = (v[j][i] - mean) * rstd * __ldg(g + c + i) + __ldg(b + c + i);
+      yr[lane + 32 * j] = pack8(o);
+    }
+    if (lane == 0) {
+      mean_out[m] = mean;
+      rstd_out[m] = rstd;
+    }
+  }
+}
+
+// dx = rstd * (g*dy - mean(g*dy) - xhat * mean(g*dy*xhat));  dres += dx (f32),
+// dres_bf = bf16(dres);  dg += sum_rows dy*xhat, db += sum_rows dy (atomics).
+template <int DV>
+__global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                     const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                                     const float* __restrict__ g, float* dres, __nv_bfloat16* dres_bf, float* dg,
+                                     float* db, int M, int D, int accumulate) {
+  const int lane = threadIdx.x & 31;
+  float adg[DV][8], adb[DV][8];
+#pragma unroll
+  for (int j = 0; j < DV; ++j)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) adg[j][i] = adb[j][i] = 0.f;
+  for (long long m = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; m < M;
+       m += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
+    const float mean = mean_in[m], rstd = rstd_in[m];
+    const uint4* xr = reinterpret_cast<const uint4*>(x + m * D);
+    const uint4* dyr = reinterpret_cast<const uint4*>(dy + m * D);
+    float xh[DV][8], gd[DV][8];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < DV; ++j) {
+      float xv[8], dv[8];
+      unpack8(xr[lane + 32 * j], xv);
+      unpack8(dyr[lane + 32 * j], dv);
+      const int c = (lane + 32 * j) * 8;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        xh[j][i] = (xv[i] - mean) * rstd;
+        gd[j][i] = dv[i] * __ldg(g + c + i);
+        s1 += gd[j][i];
+        s2 += gd[j][i] * xh[j][i];
+        adg[j][i] += dv[i] * xh[j][i];
+        adb[j][i] += dv[i];
+      }
+    }
+    const float c1 = warp_sum(s1) / D, c2 = warp_sum(s2) / D;
+    float4* rr = reinterpret_cast<float4*>(dres + m * D);
+    uint4* rb = reinterpret_cast<uint4*>(dres_bf + m * D);
+#pragma unroll
+    for (int j = 0; j < DV; ++j) {
+      float o[8];
+      const float4 r0 = accumulate ? rr[2 * (lane + 32 * j)] : make_float4(0, 0, 0, 0);
+      const float4 r1 = accumulate ? rr[2 * (lane + 32 * j) + 1] : make_float4(0, 0, 0, 0);
+      const float prev[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = prev[i] + rstd * (gd[j][i] - c1 - xh[j][i] * c2);
+      rr[2 * (lane + 32 * j)] = make_float4(o[0], o[1], o[2], o[3]);
+      rr[2 * (lane + 32 * j) + 1] = make_float4(o[4], o[5], o[6], o[7]);
+      rb[lane + 32 * j] = pack8(o);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < DV; ++j) {
+    const int c = (lane + 32 * j) * 8;
+    atomicAdd(reinterpret_cast<float4*>(dg + c), make_float4(adg[j][0], adg[j][1], adg[j][2], adg[j][3]));
+    atomicAdd(reinterpret_cast<float4*>(dg + c + 4), make_float4(adg[j][4], adg[j][5], adg[j][6], adg[j][7]));
+    atomicAdd(reinterpret_cast<float4*>(db + c), make_float4(adb[j][0], adb[j][1], adb[j][2], adb[j][3]));
+    atomicAdd(reinterpret_cast<float4*>(db + c + 4), make_float4(adb[j][4], adb[j][5], adb[j][6], adb[j][7]));
+  }
+}
+
+// out[n] (+)= sum_m x[m, n]  for bf16 x [M, N] (N % 8 == 0).  Block = 256
+// threads covering 8*32 = 256 columns x 8 row groups; float atomics per block.
+__global__ void colsum_kernel(const __nv_bfloat16* __restrict__ x, float* out, int M, int N, int rows_per_block) {
+  const int cvec = blockIdx.x * 32 + (threadIdx.x & 31);  // vector of 8 columns
+  const int rg = threadIdx.x >> 5;                        // 8 row groups
+  if (cvec * 8 >= N) return;
+  const int r0 = blockIdx.y * rows_per_block;
+  const int r1 = min(M, r0 + rows_per_block);
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int r = r0 + rg; r < r1; r += 8) {
+    float f[8];
+    unpack8(reinterpret_cast<const uint4*>(x + static_cast<long long>(r) * N)[cvec], f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] += f[i];
+  }
+  __shared__ float red[8][32][9];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red[rg][threadIdx.x & 31][i] = acc[i];
+  __syncthreads();
+  if (rg == 0) {
+#pragma unroll
+    for (int k = 1; k < 8; ++k)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += red[k][threadIdx.x & 31][i];
+    atomicAdd(reinterpret_cast<float4*>(out + cvec * 8), make_float4(acc[0], acc[1], acc[2], acc[3]));
+    atomicAdd(reinterpret_cast<float4*>(out + cvec * 8 + 4), make_float4(acc[4], acc[5], acc[6], acc[7]));
+  }
+}
+
+// AdamW (optax.adamw semantics, decoupled decay on all elements):
+//   m = b1 m + (1-b1) g;  v = b2 v + (1-b2) g^2
+//   p -= lr * ( (m / bc1) / (sqrt(v / bc2) + eps) + wd * p )
+// and the bf16 compute copy is rewritten from the updated master.
+// hyper[0..2] = lr, bc1, bc2 live in device memory so that a captured CUDA
+// graph picks up each step's schedule value.
+__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                             float* __restrict__ v, __nv_bfloat16* __restrict__ shadow, long long n4,
+                             const float* __restrict__ hyper, float b1, float b2, float eps, float wd) {
+  const float lr = hyper[0], bc1 = hyper[1], bc2 = hyper[2];
+  const float ibc1 = 1.f / bc1, ibc2 = 1.f / bc2;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float4 pp = reinterpret_cast<float4*>(p)[i];
+    const float4 gg = reinterpret_cast<const float4*>(g)[i];
+    float4 mm = reinterpret_cast<float4*>(m)[i];
+    float4 vv = reinterpret_cast<float4*>(v)[i];
+    float* P = &pp.x;
+    const float* G = &gg.x;
+    float* Mm = &mm.x;
+    float* Vv = &vv.x;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      Mm[k] = b1 * Mm[k] + (1.f - b1) * G[k];
+      Vv[k] = b2 * Vv[k] + (1.f - b2) * G[k] * G[k];
+      const float upd = (Mm[k] * ibc1) / (sqrtf(Vv[k] * ibc2) + eps) + wd * P[k];
+      P[k] -= lr * upd;
+    }
+    reinterpret_cast<float4*>(p)[i] = pp;
+    reinterpret_cast<float4*>(m)[i] = mm;
+    reinterpret_cast<float4*>(v)[i] = vv;
+    if (shadow) reinterpret_cast<uint2*>(shadow)[i] = make_uint2(pack_bf16x2(pp.x, pp.y), pack_bf16x2(pp.z, pp.w));
+  }
+}
+
+__global__ void cast_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, long long n4) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(x)[i];
+    reinterpret_cast<uint2*>(y)[i] = make_uint2(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w));
+  }
+}
+
+inline int row_grid(long long M) {
+  const long long warps = M;
+  long long blocks = (warps * 32 + 255) / 256;
+  const long long cap = static_cast<long long>(sm_count()) * 8;
+  return static_cast<int>(blocks < cap ? blocks : cap);
+}
+
+}  // namespace ew
+}  // namespace nl
+
+using namespace nl;
+
+extern "C" int nl_embed_fwd(const int* tok, const void* wte, const void* wpe, void* out, int M, int S, int D,
+                            cudaStream_t stream) {
+  if (M <= 0 || S <= 0 || D % 256) return NL_ERR_SHAPE;
+  const auto* a = static_cast<const __nv_bfloat16*>(wte);
+  const auto* b = static_cast<const __nv_bfloat16*>(wpe);
+  auto* o = static_cast<__nv_bfloat16*>(out);
+  const int grid = ew::row_grid(M);
+  switch (D / 256) {
+    case 1: ew::embed_fwd_kernel<1><<<grid, 256, 0, stream>>>(tok, a, b, o, M, S, D); break;
+    case 2: ew::embed_fwd_kernel<2><<<grid, 256, 0, stream>>>(tok, a, b, o, M, S, D); break;
+    case 4: ew::embed_fwd_kernel<4><<<grid, 256, 0, stream>>>(tok, a, b, o, M, S, D); break;
+    default: return NL_ERR_SHAPE;
+  }
+  return launch_status();
+}
+
+extern "C" int nl_embed_bwd(const int* tok, const float* dx, float* dwte, float* dwpe, int M, int S, int D,
+                            cudaStream_t stream) {
+  if (M <= 0 || S <= 0 || D % 256) return NL_ERR_SHAPE;
+  const int grid = ew::row_grid(M);
+  switch (D / 256) {
+    case 1: ew::embed_bwd_kernel<1><<<grid, 256, 0, stream>>>(tok, dx, dwte, dwpe, M, S, D); break;
+    case 2: ew::embed_bwd_kernel<2><<<grid, 256, 0, stream>>>(tok, dx, dwte, dwpe, M, S, D); break;
+    case 4: ew::embed_bwd_kernel<4><<<grid, 256, 0, stream>>>(tok, dx, dwte, dwpe, M, S, D); break;
+    default: return NL_ERR_SHAPE;
+  }
+  return launch_status();
+}
+
+extern "C" int nl_layernorm_fwd(const void* x, const float* g, const float* b, void* y, float* mean, float* rstd,
+                                int M, int D, float eps, cudaStream_t stream) {
+  if (M <= 0 || D % 256) return NL_ERR_SHAPE;
+  const auto* xi = static_cast<const __nv_bfloat16*>(x);
+  auto* yo = static_cast<__nv_bfloat16*>(y);
+  const int grid = ew::row_grid(M);
+  switch (D / 256) {
+    case 1: ew::layernorm_fwd_kernel<1><<<grid, 256, 0, stream>>>(xi, g, b, yo, mean, rstd, M, D, eps); break;
+    case 2: ew::layernorm_fwd_kernel<2><<<grid, 256, 0, stream>>>(xi, g, b, yo, mean, rstd, M, D, eps); break;
+    case 4: ew::layernorm_fwd_kernel<4><<<grid, 256, 0, stream>>>(xi, g, b, yo, mean, rstd, M, D, eps); break;
+    default: return NL_ERR_SHAPE;
+  }
+  return launch_status();
+}
+
+extern "C" int nl_layernorm_bwd(const void* dy, const void* x, const float* mean, const float* rstd, const float* g,
+                                float* dres, void* dres_bf16, float* dg, float* db, int M, int D, int accumulate,
+                                cudaStream_t stream) {
+  if (M <= 0 || D % 256) return NL_ERR_SHAPE;
+  const auto* dyi = static_cast<const __nv_bfloat16*>(dy);
+  const auto* xi = static_cast<const __nv_bfloat16*>(x);
+  auto* rb = static_cast<__nv_bfloat16*>(dres_bf16);
+  const int grid = ew::row_grid(M);
+  switch (D / 256) {
+    case 1:
+      ew::layernorm_bwd_kernel<1><<<grid, 256, 0, stream>>>(dyi, xi, mean, rstd, g, dres, rb, dg, db, M, D, accumulate);
+      break;
+    case 2:
+      ew::layernorm_bwd_kernel<2><<<grid, 256, 0, stream>>>(dyi, xi, mean, rstd, g, dres, rb, dg, db, M, D, accumulate);
+      break;
+    case 4:
+      ew::layernorm_bwd_kernel<4><<<grid, 256, 0, stream>>>(dyi, xi, mean, rstd, g, dres, rb, dg, db, M, D, accumulate);
+      break;
+    default: return NL_ERR_SHAPE;
+  }
+  return launch_status();
+}
+
+extern "C" int nl_colsum_bf16(const void* x, float* out, int M, int N, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || N % 8) return NL_ERR_SHAPE;
+  const int rows_per_block = 512;
+  dim3 grid((N / 8 + 31) / 32, (M + rows_per_block - 1) / rows_per_block);
+  ew::colsum_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), out, M, N, rows_per_block);
+  return launch_status();
+}
+
+extern "C" int nl_adamw_step(float* p, const float* g, float* m, float* v, void* shadow_bf16, long long n,
+                             const float* hyper, float b1, float b2, float eps, float wd, cudaStream_t stream) {
+  if (n <= 0 || (n & 3)) return NL_ERR_SHAPE;
+  const long long n4 = n / 4;
+  long long blocks = (n4 + 255) / 256;
+  const long long cap = static_cast<long long>(sm_count()) * 16;
+  if (blocks > cap) blocks = cap;
+  ew::adamw_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(p, g, m, v,
+                                                                   static_cast<__nv_bfloat16*>(shadow_bf16), n4,
+                                                                   hyper, b1, b2, eps, wd);
+  return launch_status();
+}
+
+extern "C" int nl_cast_bf16(const float* x, void* y, long long n, cudaStream_t stream) {
+  if (n <= 0 || (n & 3)) return NL_ERR_SHAPE;
+  const long long n4 = n / 4;
+  long long blocks = (n4 + 255) / 256;
+  const long long cap = static_cast<long long>(sm_count()) * 16;
+  if (blocks > cap) blocks = cap;
+  ew::cast_bf16_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(x, static_cast<__nv_bfloat16*>(y), n4);
+  return launch_status();
+}

@@ -59,11 +59,19 @@ struct Cfg {
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
-__device__ __forceinline__ float gelu_tanh(float a) {
-  float u = 0.7978845608028654f * (a + 0.044715f * a * a * a);
+__device__ __forceinline__ float tanh_approx(float u) {
   float t;
   asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return t;
+}
+// GELU, tanh form (the BASELINE model's FFN activation) and its derivative.
+__device__ __forceinline__ float gelu_tanh(float a) {
+  const float t = tanh_approx(0.7978845608028654f * (a + 0.044715f * a * a * a));
   return 0.5f * a * (1.f + t);
+}
+__device__ __forceinline__ float gelu_tanh_grad(float a) {
+  const float t = tanh_approx(0.7978845608028654f * (a + 0.044715f * a * a * a));
+  return 0.5f * (1.f + t) + 0.5f * a * (1.f - t * t) * 0.7978845608028654f * (1.f + 3.f * 0.044715f * a * a);
 }
 
 // Decode a work unit into (m block, n block, split index) with an M-grouped
@@ -172,6 +180,10 @@ __device__ __forceinline__ void epi_chunk(const Params& p, int row, int col0, fl
       }
     }
     return;
+  }
+  if (epi == NL_EPI_DGELU) {
+    const __nv_bfloat16* pre = p.aux + off;
+    for (int i = 0; i < 32; ++i) v[i] *= (col0 + i < p.N) ? gelu_tanh_grad(__bfloat162float(pre[i])) : 0.f;
   }
   if (epi == NL_EPI_RESID && p.resid) {
     if (p.c_bf16) {
@@ -435,6 +447,7 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
   if (epi < NL_EPI_STORE || epi > NL_EPI_LCE_GRAD) return NL_ERR_SHAPE;
   if (epi == NL_EPI_ACCUM && c_dtype != NL_F32) return NL_ERR_DTYPE;
   if (epi == NL_EPI_BIAS_GELU && (c_dtype != NL_BF16 || aux == nullptr)) return NL_ERR_DTYPE;
+  if (epi == NL_EPI_DGELU && aux == nullptr) return NL_ERR_DTYPE;
   if (epi >= NL_EPI_LCE_STATS && (ex == nullptr || ex->targets == nullptr)) return NL_ERR_WORKSPACE;
   if (epi == NL_EPI_LCE_STATS && (ex->part == nullptr || ex->tgt_logit == nullptr)) return NL_ERR_WORKSPACE;
   if (epi == NL_EPI_LCE_GRAD && (ex->lse == nullptr || c_dtype != NL_BF16)) return NL_ERR_WORKSPACE;
@@ -517,7 +530,7 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
 extern "C" int nl_gemm_ex(const void* A, int lda, int a_trans, const void* B, int ldb, int b_trans, void* C,
                           int ldc, int c_dtype, int M, int N, int K, float alpha, int epilogue, const float* bias,
                           void* aux, const void* resid, cudaStream_t stream) {
-  if (epilogue > NL_EPI_RESID) return NL_ERR_SHAPE;  // LCE epilogues go through nl_lce_*
+  if (epilogue > NL_EPI_DGELU) return NL_ERR_SHAPE;  // LCE epilogues go through nl_lce_*
   return nl::gemm_run(A, lda, a_trans, B, ldb, b_trans, C, ldc, c_dtype, M, N, K, alpha, epilogue, bias, aux,
                       resid, stream, nullptr);
 }

@@ -85,7 +85,11 @@ inline int sm_count() {
   return n;
 }
 
+// Number of kernels this library has launched (all devices, all threads).
+void count_launch();
+
 inline int launch_status() {
+  count_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? NL_OK : NL_ERR_LAUNCH;
 }

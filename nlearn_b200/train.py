@@ -1,0 +1,247 @@
+"""Data-parallel training of the BASELINE GPT on B200s: one process per GPU,
+``torch.distributed`` (NCCL over NVLink / NVSwitch) for the gradient exchange.
+
+Mirrors nlearn/train.py's step (make_train_step 328-341: loss -> grads ->
+optax update, one device boundary per step) with:
+  * synthetic Zipf(1.1) token batches standing in for fineweb-edu
+    (the container has no dataset; BASELINE configs name this stand-in);
+  * a bucketed gradient all-reduce that starts each bucket on a side stream
+    the moment the backward has produced its last gradient, overlapping the
+    rest of the backward (one flat f32 gradient buffer, no copies);
+  * fused AdamW and the warmup-cosine schedule of nlearn/train.py:487-508;
+  * atomic checkpoint / resume of {params, opt_state, step, data position}
+    (nlearn/train.py:76-99: tmp file + os.replace).
+"""
+from __future__ import annotations
+
+import os
+import time
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from .model import GPT, AdamW, FlatParams, GPTConfig, lr_schedule
+
+
+# ----------------------------------------------------------------------------- data
+def zipf_tokens(rng: np.random.Generator, shape, vocab: int, a: float = 1.1) -> np.ndarray:
+    """Zipf(a) token ids in [0, vocab): draws >= vocab are redrawn."""
+    out = rng.zipf(a, size=shape) - 1
+    bad = out >= vocab
+    while bad.any():
+        out[bad] = rng.zipf(a, size=int(bad.sum())) - 1
+        bad = out >= vocab
+    return out.astype(np.int32)
+
+
+class ZipfLoader:
+    """Per-rank stream of (inputs, targets) [B, S] int32 batches, each a
+    window of S+1 tokens.  Deterministic in (seed, rank, step)."""
+
+    def __init__(self, batch: int, seq: int, vocab: int, seed: int = 0, rank: int = 0):
+        self.batch, self.seq, self.vocab, self.seed, self.rank = batch, seq, vocab, seed, rank
+        self.step = 0
+
+    def host_batch(self, step: int | None = None):
+        s = self.step if step is None else step
+        rng = np.random.default_rng([self.seed, self.rank, s])
+        w = zipf_tokens(rng, (self.batch, self.seq + 1), self.vocab)
+        return w[:, :-1].copy(), w[:, 1:].copy()
+
+    def next(self):
+        b = self.host_batch()
+        self.step += 1
+        return b
+
+
+# ----------------------------------------------------------------------------- DP
+class BucketReducer:
+    """All-reduce (mean) of the flat gradient buffer in contiguous buckets,
+    each launched on a communication stream as soon as the backward reports
+    every parameter in it final.  Parameters are laid out in gradient-
+    production order, so buckets complete front to back."""
+
+    def __init__(self, params: FlatParams, bucket_bytes: int = 64 << 20, group=None):
+        self.P = params
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.use_avg = dist.is_initialized() and dist.get_backend(group) == "nccl"
+        cap = max(1, bucket_bytes // 4)
+        self.buckets = []  # (start, end, {names})
+        cur_names, start = set(), None
+        end = 0
+        for name, shape, _ in params.specs:
+            off, shp = params.offsets[name]
+            n = int(np.prod(shp))
+            if start is None:
+                start = off
+            cur_names.add(name)
+            end = off + n
+            if end - start >= cap:
+                self.buckets.append((start, end, cur_names))
+                cur_names, start = set(), None
+        if cur_names:
+            self.buckets.append((start, end, cur_names))
+        self.owner = {n: i for i, (_, _, ns) in enumerate(self.buckets) for n in ns}
+        self.stream = torch.cuda.Stream(device=params.device) if params.device.type == "cuda" else None
+        self._pending = None
+        self._launched = []
+
+    def begin(self):
+        self._pending = [set(ns) for (_, _, ns) in self.buckets]
+        self._launched = []
+
+    def ready(self, name: str):
+        if self.world == 1:
+            return
+        i = self.owner[name]
+        self._pending[i].discard(name)
+        if not self._pending[i]:
+            self._launch(i)
+
+    def _launch(self, i: int):
+        start, end, _ = self.buckets[i]
+        buf = self.P.grad[start:end]
+        if self.stream is not None:
+            ev = torch.cuda.Event()
+            ev.record()
+            self.stream.wait_event(ev)
+            with torch.cuda.stream(self.stream):
+                self._allreduce(buf)
+        else:
+            self._allreduce(buf)
+        self._launched.append(i)
+
+    def _allreduce(self, buf):
+        if self.use_avg:
+            dist.all_reduce(buf, op=dist.ReduceOp.AVG, group=self.group)
+        else:
+            dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.group)
+            buf.div_(self.world)
+
+    def finish(self):
+        if self.world == 1:
+            return
+        for i in range(len(self.buckets)):
+            if i not in self._launched:
+                self._launch(i)
+        if self.stream is not None:
+            torch.cuda.current_stream().wait_stream(self.stream)
+
+
+# ----------------------------------------------------------------------------- trainer
+@dataclass
+class TrainConfig:
+    batch: int = 32            # per rank
+    seq: int = 512
+    steps: int = 1000          # schedule length (decay_steps)
+    peak_lr: float = 1e-3
+    warmup: int = 200          # the BASELINE warmup; capped at steps // 5 as train.py:488
+    weight_decay: float = 0.1
+    seed: int = 0
+    bucket_mb: int = 64
+
+
+class Trainer:
+    def __init__(self, cfg: GPTConfig, tcfg: TrainConfig, device, rank: int = 0, world: int = 1, group=None):
+        self.cfg, self.tcfg = cfg, tcfg
+        self.device = torch.device(device)
+        self.rank, self.world = rank, world
+        self.P = FlatParams(cfg, self.device, seed=tcfg.seed)   # same init on every rank
+        self.model = GPT(cfg, self.P)
+        self.opt = AdamW(self.P, weight_decay=tcfg.weight_decay)
+        self.reducer = BucketReducer(self.P, tcfg.bucket_mb << 20, group)
+        self.loader = ZipfLoader(tcfg.batch, tcfg.seq, cfg.vocab, tcfg.seed, rank)
+        self.step_idx = 0
+        self.warmup = min(tcfg.warmup, tcfg.steps // 5)
+
+    def lr(self, step: int) -> float:
+        return lr_schedule(step, self.tcfg.peak_lr, self.warmup, self.tcfg.steps)
+
+    def device_batch(self, inputs, targets):
+        tok = torch.as_tensor(inputs, device=self.device)
+        tgt = torch.as_tensor(targets, device=self.device)
+        return tok, tgt
+
+    def step_on_device(self, tok: torch.Tensor, tgt: torch.Tensor) -> torch.Tensor:
+        """One optimizer step on device-resident tokens; returns the loss tensor
+        (not synchronised)."""
+        self.P.grad.zero_()
+        loss, saved = self.model.forward(tok, tgt)
+        self.reducer.begin()
+        self.model.backward(saved, on_grad_ready=self.reducer.ready)
+        self.reducer.finish()
+        self.opt.set_lr(self.lr(self.step_idx))
+        self.opt.step()
+        self.step_idx += 1
+        return loss
+
+    def train_step(self, inputs: np.ndarray, targets: np.ndarray) -> float:
+        """Host batch in, host loss out (the reference's loop body)."""
+        tok, tgt = self.device_batch(inputs, targets)
+        return float(self.step_on_device(tok, tgt))
+
+    # ------------------------------------------------------------- checkpoint
+    def save(self, path: str):
+        if self.rank != 0:
+            return
+        state = {"params": self.P.state_dict(), "step": self.step_idx, "opt_t": self.opt.t,
+                 "loader_step": self.loader.step, "config": self.cfg.__dict__, "train": self.tcfg.__dict__}
+        tmp = path + ".tmp"
+        torch.save({k: (v if not isinstance(v, dict) else {kk: (vv.cpu() if torch.is_tensor(vv) else vv)
+                                                           for kk, vv in v.items()}) for k, v in state.items()},
+                   tmp)
+        os.replace(tmp, path)
+
+    def load(self, path: str):
+        state = torch.load(path, map_location="cpu", weights_only=False)
+        self.P.load_state_dict({k: v.to(self.device) for k, v in state["params"].items()})
+        self.step_idx = state["step"]
+        self.opt.t = state["opt_t"]
+        self.loader.step = state["loader_step"]
+
+
+def init_distributed():
+    """(rank, world, local_rank) from torchrun's environment; NCCL when CUDA."""
+    if "RANK" not in os.environ or int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        return 0, 1, 0
+    backend = "nccl" if torch.cuda.is_available() else "gloo"
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if backend == "nccl":
+        torch.cuda.set_device(local)
+    dist.init_process_group(backend=backend, timeout=__import__("datetime").timedelta(seconds=120))
+    return dist.get_rank(), dist.get_world_size(), local
+
+
+def main(argv=None):  # pragma: no cover - CLI
+    import argparse
+    ap = argparse.ArgumentParser(description="nlearn-b200 data-parallel training (synthetic Zipf tokens)")
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--seq", type=int, default=512)
+    ap.add_argument("--lr", type=float, default=1e-3)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--checkpoint", default=None)
+    ap.add_argument("--resume", action="store_true")
+    a = ap.parse_args(argv)
+    rank, world, local = init_distributed()
+    cfg = GPTConfig(max_seq=max(512, a.seq))
+    tr = Trainer(cfg, TrainConfig(batch=a.batch, seq=a.seq, steps=a.steps, peak_lr=a.lr, seed=a.seed),
+                 f"cuda:{local}", rank, world)
+    if a.resume and a.checkpoint and os.path.exists(a.checkpoint):
+        tr.load(a.checkpoint)
+    while tr.step_idx < a.steps:
+        t0 = time.time()
+        loss = tr.train_step(*tr.loader.next())
+        if rank == 0:
+            print(f"step {tr.step_idx} loss {loss:.4f} {time.time() - t0:.3f}s", flush=True)
+    if a.checkpoint:
+        tr.save(a.checkpoint)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":  # pragma: no cover
+    main()

@@ -1,0 +1,91 @@
+"""CPU oracle of the BASELINE GPT training step — TEST INFRASTRUCTURE ONLY.
+
+A float32 PyTorch-on-CPU restatement (autograd for the backward) of the model
+and optimizer the headline metric trains:
+  * model: nlearn's d512 / 8 heads / 4 pre-LN blocks / GELU(tanh) 4x FFN /
+    learned positions / untied head (the metric's configuration; block
+    structure nlearn/model.py:315-324, attention nlearn/attention.py:138-156,
+    LayerNorm + GELU as iree_metal/kernels/test/bf16_metal_test.py:6-12);
+  * loss: mean softmax CE of the next token (nlearn/train.py:270-285);
+  * optimizer: optax.adamw(b1 .9, b2 .999, eps 1e-8, wd .1 on every leaf)
+    with warmup_cosine_decay_schedule (nlearn/train.py:487-508), written out
+    from optax's published update rule.
+Parity of the optimizer is unpinned by any reference test (optax is a
+third-party dependency absent here); the formulas are restated.
+
+Parameters are keyed by the same names as nlearn_b200.model.param_specs so
+tests can load the exact initial weights of the GPU run.  Only tests/,
+__graft_entry__.smoke() and bench.py's CPU-baseline leg use this module.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+
+class OracleGPT:
+    def __init__(self, params: dict, n_layers=4, n_heads=8, vocab=50257, eps=1e-5):
+        # params: name -> f32 CPU tensor (head.w may be column-padded)
+        self.p = {k: v.detach().clone().float().requires_grad_(True) for k, v in params.items()}
+        self.L, self.H, self.V, self.eps = n_layers, n_heads, vocab, eps
+
+    def loss(self, tok: torch.Tensor, tgt: torch.Tensor) -> torch.Tensor:
+        p, H = self.p, self.H
+        B, S = tok.shape
+        D = p["wte"].shape[1]
+        x = p["wte"][tok.long()] + p["wpe"][:S][None]
+        mask = torch.triu(torch.ones(S, S, dtype=torch.bool), 1)
+        for layer in range(self.L):
+            q = f"blocks.{layer}."
+            h = F.layer_norm(x, (D,), p[q + "ln1.g"], p[q + "ln1.b"], self.eps)
+            qkv = (h @ p[q + "wqkv"]).view(B, S, 3, H, D // H)
+            Q, K, V = (qkv[:, :, i].transpose(1, 2) for i in range(3))
+            sc = (Q @ K.transpose(-1, -2)) / math.sqrt(D // H)
+            sc = sc.masked_fill(mask, float("-inf"))
+            o = (torch.softmax(sc, -1) @ V).transpose(1, 2).reshape(B, S, D)
+            x = x + o @ p[q + "wo"]
+            h = F.layer_norm(x, (D,), p[q + "ln2.g"], p[q + "ln2.b"], self.eps)
+            u = F.gelu(h @ p[q + "w1"] + p[q + "b1"], approximate="tanh")
+            x = x + u @ p[q + "w2"] + p[q + "b2"]
+        h = F.layer_norm(x, (D,), p["lnf.g"], p["lnf.b"], self.eps)
+        logits = h @ p["head.w"][:, :self.V]
+        return F.cross_entropy(logits.reshape(-1, self.V), tgt.reshape(-1).long())
+
+    def grads(self):
+        return {k: (v.grad if v.grad is not None else torch.zeros_like(v)) for k, v in self.p.items()}
+
+
+def lr_at(step, peak, warmup, decay_steps):
+    """optax.warmup_cosine_decay_schedule(0, peak, warmup, decay_steps, peak/10)."""
+    end = peak / 10
+    if warmup > 0 and step < warmup:
+        return peak * step / warmup
+    if decay_steps <= warmup:
+        return end
+    frac = min(max(step - warmup, 0), decay_steps - warmup) / (decay_steps - warmup)
+    return end + (peak - end) * 0.5 * (1 + math.cos(math.pi * frac))
+
+
+class OracleAdamW:
+    """optax.adamw update: m, v EMAs; bias-corrected; decoupled decay."""
+
+    def __init__(self, params: dict, b1=0.9, b2=0.999, eps=1e-8, wd=0.1):
+        self.params = params
+        self.b1, self.b2, self.eps, self.wd = b1, b2, eps, wd
+        self.m = {k: torch.zeros_like(v) for k, v in params.items()}
+        self.v = {k: torch.zeros_like(v) for k, v in params.items()}
+        self.t = 0
+
+    @torch.no_grad()
+    def step(self, lr):
+        self.t += 1
+        bc1, bc2 = 1 - self.b1 ** self.t, 1 - self.b2 ** self.t
+        for k, p in self.params.items():
+            g = p.grad if p.grad is not None else torch.zeros_like(p)
+            self.m[k].mul_(self.b1).add_(g, alpha=1 - self.b1)
+            self.v[k].mul_(self.b2).addcmul_(g, g, value=1 - self.b2)
+            upd = (self.m[k] / bc1) / ((self.v[k] / bc2).sqrt() + self.eps) + self.wd * p
+            p.sub_(lr * upd)
+            p.grad = None
