@@ -39,7 +39,8 @@ typedef enum {
   NL_ERR_LAUNCH = -3,    /* kernel launch failed                            */
   NL_ERR_CUDA = -4,      /* CUDA runtime / driver entry point unavailable   */
   NL_ERR_DTYPE = -5,     /* unsupported dtype code                          */
-  NL_ERR_WORKSPACE = -6  /* workspace missing or too small                  */
+  NL_ERR_WORKSPACE = -6, /* workspace missing or too small                  */
+  NL_ERR_TOO_LARGE = -7  /* problem exceeds a fixed built-in scratch limit   */
 } nl_status;
 
 typedef enum { NL_F32 = 0, NL_BF16 = 1 } nl_dtype;
@@ -132,6 +133,21 @@ NL_API int nl_flash_attention_bwd_dq(const void* Q, const void* K, const void* V
 NL_API int nl_flash_attention_bwd_dkdv(const void* Q, const void* K, const void* V, const void* dO,
                                        const float* L, const float* D, void* dK, void* dV, int n, int s, int d,
                                        cudaStream_t stream);
+
+/* Allocation-free variant of nl_flash_attention_bwd, for callers that cannot
+ * allocate device memory (no workspace argument).  No counterpart in the
+ * reference.  Its scratch (dQ accumulator and D) is a fixed array inside the
+ * library, sized for n * s <= nl_flash_attention_bwd_noalloc_max_rows()
+ * (131072 rows = 32.5 MiB, held on every device that loads the library until
+ * the process exits); larger problems return NL_ERR_TOO_LARGE.  The first
+ * call on each device resolves the array's device address (make that first
+ * call before any stream capture).  All calls share the one array: calls
+ * that overlap on the GPU (different streams, threads) race and must be
+ * serialised by the caller.  Same results as nl_flash_attention_bwd. */
+NL_API long long nl_flash_attention_bwd_noalloc_max_rows(void);
+NL_API int nl_flash_attention_bwd_noalloc(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+                                          const float* L, void* dQ, void* dK, void* dV, int n, int s, int d,
+                                          cudaStream_t stream);
 
 /* Strided forms used by the training step: activations addressed as
  * [B][H][s][64] with element strides (q_s, q_h, q_b) for Q, K, V, dQ, dK, dV

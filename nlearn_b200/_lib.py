@@ -18,7 +18,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().with_name("libnl_ops.so")
 
 STATUS = {0: "NL_OK", -1: "NL_ERR_SHAPE", -2: "NL_ERR_ALIGN", -3: "NL_ERR_LAUNCH", -4: "NL_ERR_CUDA",
-          -5: "NL_ERR_DTYPE", -6: "NL_ERR_WORKSPACE"}
+          -5: "NL_ERR_DTYPE", -6: "NL_ERR_WORKSPACE", -7: "NL_ERR_TOO_LARGE"}
 F32, BF16 = 0, 1
 EPI_STORE, EPI_ACCUM, EPI_BIAS, EPI_BIAS_GELU, EPI_RESID, EPI_DGELU = 0, 1, 2, 3, 4, 5
 
@@ -39,6 +39,8 @@ SIGNATURES: dict[str, list] = {
     "nl_flash_attention_bwd": [c_void_p] * 11 + [c_int, c_int, c_int, c_void_p],
     "nl_flash_attention_bwd_dq": [c_void_p] * 8 + [c_int, c_int, c_int, c_void_p],
     "nl_flash_attention_bwd_dkdv": [c_void_p] * 8 + [c_int, c_int, c_int, c_void_p],
+    "nl_flash_attention_bwd_noalloc_max_rows": [],
+    "nl_flash_attention_bwd_noalloc": [c_void_p] * 9 + [c_int, c_int, c_int, c_void_p],
     "nl_flash_attention_fwd_strided": [c_void_p] * 3 + [c_longlong] * 3 + [c_void_p] + [c_longlong] * 3 +
                                       [c_void_p, c_int, c_int, c_int, c_int, c_void_p],
     "nl_flash_attention_bwd_strided": [c_void_p] * 3 + [c_longlong] * 3 + [c_void_p] * 2 + [c_longlong] * 3 +
@@ -56,7 +58,8 @@ SIGNATURES: dict[str, list] = {
     "nl_lce_bwd": [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
                    c_int, c_int, c_void_p, ctypes.c_size_t, c_int, c_int, c_int, c_int, c_void_p],
 }
-_RESTYPE = {"nl_version": ctypes.c_char_p, "nl_launch_count": c_longlong, "nl_lce_workspace_bytes": ctypes.c_size_t}
+_RESTYPE = {"nl_version": ctypes.c_char_p, "nl_launch_count": c_longlong,
+            "nl_flash_attention_bwd_noalloc_max_rows": c_longlong, "nl_lce_workspace_bytes": ctypes.c_size_t}
 
 
 class NlError(RuntimeError):

@@ -763,6 +763,51 @@ extern "C" int nl_flash_attention_bwd_dkdv(const void* Q, const void* K, const v
                        dV, nullptr, n, 1, s, d, stream);
 }
 
+// ----------------------------------------------------------------------------
+// Allocation-free backward.  Some callers cannot allocate device memory at the
+// point where they run the backward (for example a host framework that hands
+// over only its own input / output buffers, or code that runs where
+// cudaMalloc is not permitted).  For them the backward's scratch — the f32 dQ
+// accumulator [rows, 64] and the f32 D = rowsum(dO*O) vector [rows] — lives in
+// this fixed, file-scope device array instead of a caller workspace.
+// Limit: rows = n * s <= kNoAllocMaxRows (131072, e.g. 256 heads x 512 or
+// 32 heads x 4096), i.e. 32.5 MiB held on every device that loads the library,
+// for the life of the process.
+constexpr long long kNoAllocMaxRows = 131072;
+static __device__ __align__(256) float g_bwd_scratch[kNoAllocMaxRows * (64 + 1)];
+
+namespace {
+// Device address of g_bwd_scratch, resolved once per device on that device's
+// first call (host code may not use the symbol itself as a pointer).
+float* noalloc_scratch() {
+  constexpr int kMaxDev = 64;
+  static float* addr[kMaxDev] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return nullptr;
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_bwd_scratch) != cudaSuccess) return nullptr;
+    addr[dev] = static_cast<float*>(p);
+  }
+  return addr[dev];
+}
+}  // namespace
+
+extern "C" long long nl_flash_attention_bwd_noalloc_max_rows(void) { return kNoAllocMaxRows; }
+
+extern "C" int nl_flash_attention_bwd_noalloc(const void* Q, const void* K, const void* V, const void* O,
+                                              const void* dO, const float* L, void* dQ, void* dK, void* dV, int n,
+                                              int s, int d, cudaStream_t stream) {
+  if (n <= 0 || s <= 0) return NL_ERR_SHAPE;
+  if (static_cast<long long>(n) * s > kNoAllocMaxRows) return NL_ERR_TOO_LARGE;
+  if (!O) return NL_ERR_SHAPE;
+  float* base = noalloc_scratch();
+  if (!base) return NL_ERR_CUDA;
+  float* dqacc = base;                                   // [rows, 64], zeroed by the pre-pass
+  float* D = base + kNoAllocMaxRows * 64;                // [rows], written by the pre-pass
+  return nl::flash_bwd(Q, K, V, contiguous(s), O, dO, contiguous(s), L, D, dQ, dK, dV, dqacc, n, 1, s, d, stream);
+}
+
 extern "C" int nl_flash_attention_fwd_strided(const void* Q, const void* K, const void* V, long long q_s,
                                               long long q_h, long long q_b, void* O, long long o_s, long long o_h,
                                               long long o_b, float* L, int B, int H, int s, int d,
