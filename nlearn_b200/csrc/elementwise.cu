@@ -179,13 +179,25 @@ __global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const
       rb[lane + 32 * j] = pack8(o);
     }
   }
+  // Block-level reduction of the per-warp gamma / beta partials in shared
+  // memory, then one atomic per column per block (few blocks, so the global
+  // atomics do not serialise on the D hot addresses).
+  __shared__ float red[8][DV * 256];
+  const int w = threadIdx.x >> 5;
 #pragma unroll
-  for (int j = 0; j < DV; ++j) {
-    const int c = (lane + 32 * j) * 8;
-    atomicAdd(reinterpret_cast<float4*>(dg + c), make_float4(adg[j][0], adg[j][1], adg[j][2], adg[j][3]));
-    atomicAdd(reinterpret_cast<float4*>(dg + c + 4), make_float4(adg[j][4], adg[j][5], adg[j][6], adg[j][7]));
-    atomicAdd(reinterpret_cast<float4*>(db + c), make_float4(adb[j][0], adb[j][1], adb[j][2], adb[j][3]));
-    atomicAdd(reinterpret_cast<float4*>(db + c + 4), make_float4(adb[j][4], adb[j][5], adb[j][6], adb[j][7]));
+  for (int which = 0; which < 2; ++which) {
+#pragma unroll
+    for (int j = 0; j < DV; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) red[w][(lane + 32 * j) * 8 + i] = which ? adb[j][i] : adg[j][i];
+    __syncthreads();
+    for (int c = threadIdx.x; c < D; c += blockDim.x) {
+      float t = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t += red[k][c];
+      atomicAdd((which ? db : dg) + c, t);
+    }
+    __syncthreads();
   }
 }
 
@@ -324,7 +336,8 @@ extern "C" int nl_layernorm_bwd(const void* dy, const void* x, const float* mean
   const auto* dyi = static_cast<const __nv_bfloat16*>(dy);
   const auto* xi = static_cast<const __nv_bfloat16*>(x);
   auto* rb = static_cast<__nv_bfloat16*>(dres_bf16);
-  const int grid = ew::row_grid(M);
+  int grid = ew::row_grid(M);
+  if (grid > 2 * sm_count()) grid = 2 * sm_count();  // few blocks: cheap gamma/beta atomics
   switch (D / 256) {
     case 1:
       ew::layernorm_bwd_kernel<1><<<grid, 256, 0, stream>>>(dyi, xi, mean, rstd, g, dres, rb, dg, db, M, D, accumulate);
@@ -342,7 +355,7 @@ extern "C" int nl_layernorm_bwd(const void* dy, const void* x, const float* mean
 
 extern "C" int nl_colsum_bf16(const void* x, float* out, int M, int N, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || N % 8) return NL_ERR_SHAPE;
-  const int rows_per_block = 512;
+  const int rows_per_block = 64;
   dim3 grid((N / 8 + 31) / 32, (M + rows_per_block - 1) / rows_per_block);
   ew::colsum_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), out, M, N, rows_per_block);
   return launch_status();

@@ -6,15 +6,17 @@
 // MN-major in global memory, so dX = dY.W^T and dW = X^T.dY read the forward
 // tensors in place.
 //
-// CTA = 6 warps, one CTA per SM, persistent over output tiles:
+// CTA = 10 warps, one CTA per SM, persistent over output tiles:
 //   warp 0      TMA producer: A/B k-blocks (64 deep) into a STAGES-deep ring
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2..5  epilogue: tcgen05.ld of the f32 accumulator (one TMEM lane =
+//   warps 2..9  epilogue (two warps per TMEM lane quarter, half the columns each): tcgen05.ld of the f32 accumulator (one TMEM lane =
 //               one output row per thread), fused bias / GELU / residual /
 //               accumulate, vectorised stores
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
 // of tile i overlaps the main loop of tile i+1.  Split-K (for the long-K,
 // few-tile dW GEMMs) accumulates with vector float atomics.
+#include <stdlib.h>
+
 #include "sm100.cuh"
 #include "host_common.h"
 #include "gemm.h"
@@ -24,7 +26,10 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle row of bf16
-constexpr int kThreads = 6 * 32;
+// 2 control warps + 8 epilogue warps (two per TMEM lane quarter, each taking
+// half of the tile's columns) so the epilogue keeps pace with the MMAs.
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = (2 + kEpiWarps) * 32;
 
 struct Params {
   int M, N, K;
@@ -40,12 +45,13 @@ struct Params {
   int* err;
   // fused LM-head cross-entropy epilogues
   const int* targets;   // [M] target column (global vocab index)
-  float2* part;         // LCE_STATS: [tiles_n, M] per-tile (max, sum 2^(y-max)), base-2 units
+  float2* part;         // LCE_STATS: [2*tiles_n, M] per half-tile (max, sum exp(x-max)), natural units
   float* tgt_logit;     // LCE_STATS: [M] logit of the target column
   const float* lse;     // LCE_GRAD: [M] natural-log logsumexp
   const float* gptr;    // LCE_GRAD: optional device scalar multiplying grad_scale
   float grad_scale;     // LCE_GRAD: dlogits multiplier (1/M for a mean loss)
   int v_valid;          // columns >= v_valid are vocabulary padding (masked)
+  int epi_warps;        // 4 or 8 active epilogue warps
   int col_offset;       // global vocab index of this launch's column 0
 };
 
@@ -92,9 +98,11 @@ __device__ __forceinline__ void decode_unit(const Params& p, int u, int& mb, int
 
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Online (max, sum-exp) of 32 logits of one row, base 2; padding columns masked.
+// Online (max, sum-exp) of 32 logits of one row, the max kept in base-2 units
+// (y = x log2 e, so each term is one MUFU ex2); padding columns masked.  (A
+// natural-units variant with a separate max pass measured 20-40 % slower.)
 __device__ __forceinline__ void lce_stats_chunk(const Params& p, int row, int col0, const float (&v)[32], float& m,
-                                                float& s, float& tl, int t) {
+                                                   float& s, float& tl, int t) {
   float y[32];
   float mx = -INFINITY;
 #pragma unroll
@@ -276,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull_bar[i], 1);
-      mbar_init(&tempty_bar[i], 4 * 32);
+      mbar_init(&tempty_bar[i], p.epi_warps * 32);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -363,10 +371,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    // with 8 epilogue warps each takes half of the tile's columns; with 4 the
+    // warps 6..9 idle and warps 2..5 take all columns
+    const int split = p.epi_warps / 4;
+    const int half = (warp - 2) >> 2;
     int acc = 0;
     uint32_t acc_ph = 0;
-    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+    for (int u = blockIdx.x; half < split && u < num_units; u += gridDim.x) {
       int mb, nb, sk;
       decode_unit(p, u, mb, nb, sk);
       if (!mbar_wait(&tfull_bar[acc], acc_ph, ab)) break;
@@ -384,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = half * (BN / 32 / split); c < (half + 1) * (BN / 32 / split); ++c) {
         const int col0 = nb * BN + c * 32;
         if (col0 >= p.N) break;  // warp-uniform
         uint32_t r[32];
@@ -398,8 +410,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         else lce_grad_chunk(p, row, col0, v, lse2, t, gsc);
       }
       if (p.epi == NL_EPI_LCE_STATS && row < p.M) {
-        p.part[(long long)nb * p.M + row] = make_float2(m, ssum);
-        if (t >= nb * BN && t < nb * BN + BN && t < p.N) p.tgt_logit[row] = tl;
+        m *= 0.6931471805599453f;  // base-2 max -> natural units
+        p.part[(long long)(2 * nb + half) * p.M + row] = make_float2(m, ssum);
+        if (split == 1) p.part[(long long)(2 * nb + 1) * p.M + row] = make_float2(-INFINITY, 0.f);
+        const int c0 = nb * BN + half * (BN / split);
+        if (t >= c0 && t < c0 + BN / split && t < p.N) p.tgt_logit[row] = tl;
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
@@ -469,6 +484,14 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
   p.resid = resid;
   p.err = device_error_word();
   p.num_kb = (K + BK - 1) / BK;
+  {
+    static int ew = -1;
+    if (ew < 0) {
+      const char* e = getenv("NL_GEMM_EPI_WARPS");
+      ew = (e && atoi(e) == 4) ? 4 : 8;
+    }
+    p.epi_warps = ew;
+  }
   if (ex) {
     p.targets = ex->targets;
     p.part = ex->part;

@@ -9,7 +9,7 @@ namespace nl {
 // Extra epilogue inputs for NL_EPI_LCE_STATS / NL_EPI_LCE_GRAD.
 struct GemmExtra {
   const int* targets = nullptr;   // [M] global vocabulary index of each row's target
-  float2* part = nullptr;         // STATS: [ceil(N/256), M] per-tile (max, sum-exp), base 2
+  float2* part = nullptr;         // STATS: [2*ceil(N/256), M] per half-tile (max, sum-exp)
   float* tgt_logit = nullptr;     // STATS: [M] target logit
   const float* lse = nullptr;     // GRAD: [M] logsumexp (natural log)
   const float* gptr = nullptr;    // GRAD: optional device scalar multiplier

@@ -27,6 +27,7 @@ namespace lce {
 
 constexpr int kTileN = 256;  // the STATS epilogue runs with 256-wide tiles
 constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ float ex2f(float x) {
   float y;
@@ -34,7 +35,8 @@ __device__ __forceinline__ float ex2f(float x) {
   return y;
 }
 
-// One thread per row: combine the per-tile partials (coalesced across rows).
+// One thread per row: combine the per-half-tile partials (max in natural units,
+// sum of exp(x - max)), coalesced across rows.
 __global__ void lce_reduce_kernel(const float2* __restrict__ part, const float* __restrict__ tgt_logit,
                                   const int* __restrict__ targets, float* __restrict__ loss, float* __restrict__ lse,
                                   int M, int tiles, int V) {
@@ -46,13 +48,13 @@ __global__ void lce_reduce_kernel(const float2* __restrict__ part, const float* 
     const float2 p = part[(long long)t * M + row];
     if (p.x == -INFINITY) continue;
     if (p.x > m) {
-      s = s * ex2f(m - p.x) + p.y;
+      s = s * ex2f((m - p.x) * kLog2e) + p.y;
       m = p.x;
     } else {
-      s += p.y * ex2f(p.x - m);
+      s += p.y * ex2f((p.x - m) * kLog2e);
     }
   }
-  const float l = (m + __log2f(s)) * kLn2;
+  const float l = m + __log2f(s) * kLn2;
   lse[row] = l;
   const int t = targets[row];
   loss[row] = l - ((t >= 0 && t < V) ? tgt_logit[row] : 0.f);
@@ -66,7 +68,7 @@ struct Layout {
 
 inline Layout layout(long long M, long long V, long long chunk) {
   Layout L;
-  const long long tiles = (V + kTileN - 1) / kTileN;
+  const long long tiles = 2 * ((V + kTileN - 1) / kTileN);  // one partial per tile half
   L.part = 0;
   L.tgt = align256(L.part + static_cast<size_t>(tiles * M) * sizeof(float2));
   L.dl = align256(L.tgt + static_cast<size_t>(M) * sizeof(float));
@@ -100,7 +102,7 @@ extern "C" int nl_lce_fwd(const void* X, int ldx, const void* W, int ldw, const 
   int st = gemm_run(X, ldx, 0, W, ldw, 0, nullptr, 0, NL_F32, M, V, D, 1.f, NL_EPI_LCE_STATS, nullptr, nullptr,
                     nullptr, stream, &ex);
   if (st) return st;
-  const int tiles = (V + lce::kTileN - 1) / lce::kTileN;
+  const int tiles = 2 * ((V + lce::kTileN - 1) / lce::kTileN);
   lce::lce_reduce_kernel<<<(M + 127) / 128, 128, 0, stream>>>(ex.part, ex.tgt_logit, targets, loss, lse, M, tiles,
                                                                V);
   return launch_status();

@@ -99,7 +99,7 @@ def cross_entropy(logits: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
 
 # Vocabulary chunk of the fused backward (the reference's NLEARN_LCE_CHUNK,
 # cross_entropy.py:91); rounded to a multiple of 64 columns.
-_LCE_CHUNK = max(64, int(os.environ.get("NLEARN_LCE_CHUNK", "8192")) // 64 * 64)
+_LCE_CHUNK = max(64, int(os.environ.get("NLEARN_LCE_CHUNK", "16384")) // 64 * 64)
 
 
 def _lce_operands(X, W):
