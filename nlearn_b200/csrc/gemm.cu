@@ -16,6 +16,7 @@
 // of tile i overlaps the main loop of tile i+1.  Split-K (for the long-K,
 // few-tile dW GEMMs) accumulates with vector float atomics.
 #include <stdlib.h>
+#include <string.h>
 
 #include "sm100.cuh"
 #include "host_common.h"
@@ -30,6 +31,7 @@ constexpr int BK = 64;  // one 128-byte swizzle row of bf16
 // half of the tile's columns) so the epilogue keeps pace with the MMAs.
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
+constexpr int kStagingBytes = kEpiWarps * 4096;  // one 32x32 f32 block per epilogue warp
 
 struct Params {
   int M, N, K;
@@ -52,6 +54,8 @@ struct Params {
   float grad_scale;     // LCE_GRAD: dlogits multiplier (1/M for a mean loss)
   int v_valid;          // columns >= v_valid are vocabulary padding (masked)
   int epi_warps;        // 4 or 8 active epilogue warps
+  int tma_out;          // 1: outputs leave through staged TMA stores (tmC / tmX valid)
+  int group_m;          // M tiles per raster group
   int col_offset;       // global vocab index of this launch's column 0
 };
 
@@ -62,7 +66,7 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN == 256) ? 4 : 6;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + kStagingBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 __device__ __forceinline__ float tanh_approx(float u) {
@@ -86,7 +90,7 @@ __device__ __forceinline__ void decode_unit(const Params& p, int u, int& mb, int
   const int tiles = p.tiles_m * p.tiles_n;
   sk = u / tiles;
   int t = u - sk * tiles;
-  constexpr int G = 16;
+  const int G = p.group_m;
   const int per_group = G * p.tiles_n;
   const int g = t / per_group;
   const int first_m = g * G;
@@ -147,6 +151,17 @@ __device__ __forceinline__ void lce_grad_chunk(const Params& p, int row, int col
       const unsigned short h = (i & 1) ? (w >> 16) : (w & 0xffff);
       cb[i] = __ushort_as_bfloat16(h);
     }
+  }
+}
+
+// dlogits values (f32) of 32 columns for the staged-store path; padding -> 0.
+__device__ __forceinline__ void lce_grad_values(const Params& p, int col0, float (&v)[32], float lse2, int t,
+                                                float scale) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int c = col0 + i;
+    const float pr = ex2_approx(v[i] * kLog2e - lse2);
+    v[i] = (c < p.v_valid) ? (pr - (c == t ? 1.f : 0.f)) * scale : 0.f;
   }
 }
 
@@ -258,14 +273,204 @@ __device__ __forceinline__ void epi_chunk(const Params& p, int row, int col0, fl
   }
 }
 
+// ---------------------------------------------------------------- TMA-store epilogue
+// A warp owns a 32-row x 32-column block per chunk.  Row-per-thread stores to
+// global memory would touch 32 lines per instruction; instead the block is
+// written to this warp's 4 KB staging slot in the swizzled layout a TMA store
+// expects (f32: 128 B rows, 128-byte swizzle; bf16: 64 B rows, 64-byte
+// swizzle, so 8 consecutive lanes hit 8 distinct bank groups) and one lane
+// issues a bulk tensor store (or an atomic bulk reduce-add for accumulating
+// epilogues, which also makes split-K safe without per-element atomics).
+// Rows >= M and columns >= N of the box are clipped by the TMA unit.
+__device__ __forceinline__ void stage_f32(uint8_t* slot, int lane, const float (&v)[32]) {
+  const uint32_t base = smem_u32(slot) + lane * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t a = base + ((j ^ (lane & 7)) << 4);
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(v[4 * j]), "f"(v[4 * j + 1]),
+                 "f"(v[4 * j + 2]), "f"(v[4 * j + 3])
+                 : "memory");
+  }
+}
+__device__ __forceinline__ void stage_bf16(uint8_t* slot, int lane, const float (&v)[32]) {
+  const uint32_t base = smem_u32(slot) + lane * 64;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t a = base + ((j ^ ((lane >> 1) & 3)) << 4);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(pack_bf16x2(v[8 * j], v[8 * j + 1])),
+                 "r"(pack_bf16x2(v[8 * j + 2], v[8 * j + 3])), "r"(pack_bf16x2(v[8 * j + 4], v[8 * j + 5])),
+                 "r"(pack_bf16x2(v[8 * j + 6], v[8 * j + 7]))
+                 : "memory");
+  }
+}
+// Make the staged block visible to the TMA unit and issue the store from lane 0.
+__device__ __forceinline__ void flush_block(const CUtensorMap* m, uint8_t* slot, int lane, int col0, int row0,
+                                            bool reduce) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (reduce) tma_reduce_add_2d(m, slot, col0, row0);
+    else tma_store_2d(m, slot, col0, row0);
+    bulk_commit();
+  }
+}
+// Before rewriting the slot: the previous store must have read it.
+__device__ __forceinline__ void slot_reuse_wait(int lane) {
+  if (lane == 0) bulk_wait_read_all();
+  __syncwarp();
+}
+
+__device__ __forceinline__ void epi_chunk_tma(const Params& p, const CUtensorMap* tmC, const CUtensorMap* tmX,
+                                              uint8_t* slot, int lane, int row, int row0, int col0, float (&v)[32]) {
+  const bool in = row < p.M;
+  const int epi = p.epi;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] *= p.alpha;
+  if (p.bias && (epi == NL_EPI_BIAS || epi == NL_EPI_BIAS_GELU || epi == NL_EPI_RESID)) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] += (col0 + i < p.N) ? __ldg(p.bias + col0 + i) : 0.f;
+  }
+  const long long off = (long long)row * p.ldc + col0;
+  const bool full = col0 + 32 <= p.N;
+  slot_reuse_wait(lane);
+  if (epi == NL_EPI_BIAS_GELU) {  // aux = pre-activation, C = gelu(pre): two bf16 halves of the slot
+    stage_bf16(slot, lane, v);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+    stage_bf16(slot + 2048, lane, v);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmX, slot, col0, row0);
+      tma_store_2d(tmC, slot + 2048, col0, row0);
+      bulk_commit();
+    }
+    return;
+  }
+  if (epi == NL_EPI_DGELU && in) {
+    const __nv_bfloat16* pre = p.aux + off;
+    if (full && (p.ldc & 7) == 0) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 u = reinterpret_cast<const uint4*>(pre)[j];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __bfloat1622float2(h[k]);
+          v[8 * j + 2 * k] *= gelu_tanh_grad(f.x);
+          v[8 * j + 2 * k + 1] *= gelu_tanh_grad(f.y);
+        }
+      }
+    } else {
+      for (int i = 0; i < 32; ++i) v[i] *= (col0 + i < p.N) ? gelu_tanh_grad(__bfloat162float(pre[i])) : 0.f;
+    }
+  }
+  if (epi == NL_EPI_RESID && p.resid && in) {
+    if (p.c_bf16) {
+      const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(p.resid) + off;
+      if (full && (p.ldc & 7) == 0) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 u = reinterpret_cast<const uint4*>(rb)[j];
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = __bfloat1622float2(h[k]);
+            v[8 * j + 2 * k] += f.x;
+            v[8 * j + 2 * k + 1] += f.y;
+          }
+        }
+      } else {
+        for (int i = 0; i < 32; ++i) v[i] += (col0 + i < p.N) ? __bfloat162float(rb[i]) : 0.f;
+      }
+    } else {
+      const float* rf = reinterpret_cast<const float*>(p.resid) + off;
+      for (int i = 0; i < 32; ++i) v[i] += (col0 + i < p.N) ? rf[i] : 0.f;
+    }
+  }
+  if (p.c_bf16) stage_bf16(slot, lane, v);
+  else stage_f32(slot, lane, v);
+  flush_block(tmC, slot, lane, col0, row0, epi == NL_EPI_ACCUM);
+}
+
+// Epilogue warps (2..9): drain each finished accumulator from TMEM, apply the
+// fused epilogue, and release the TMEM buffer by arriving on tempty (a local
+// barrier, or the pair leader's via its cluster address).  `unit_rows` is the
+// M extent of one work unit (128, or 256 for a CTA pair) and `row_off` this
+// CTA's first row inside it.
+template <int BN>
+__device__ __forceinline__ void epilogue_role(const Params& p, uint32_t tmem_base, uint64_t* tfull_bar,
+                                              uint32_t tempty0, uint32_t tempty1, bool remote, int unit_rows,
+                                              int row_off, const Abort& ab, const CUtensorMap* tmC,
+                                              const CUtensorMap* tmX, uint8_t* staging) {
+  uint8_t* slot = staging + (warp_id() - 2) * 4096;
+  const int warp = warp_id(), lane = lane_id();
+  const int num_units = p.tiles_m * p.tiles_n * p.split_k;
+  const int cta_unit0 = remote ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int cta_stride = remote ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int q = warp & 3;             // TMEM lane quarter this warp may access
+  // with 8 epilogue warps each takes half of the tile's columns; with 4 the
+  // warps 6..9 idle and warps 2..5 take all columns
+  const int split = p.epi_warps / 4;
+  const int half = (warp - 2) >> 2;
+  int acc = 0;
+  uint32_t acc_ph = 0;
+  for (int u = cta_unit0; half < split && u < num_units; u += cta_stride) {
+    int mb, nb, sk;
+    decode_unit(p, u, mb, nb, sk);
+    if (!mbar_wait(&tfull_bar[acc], acc_ph, ab)) break;
+    tc_fence_after();
+    const int row = mb * unit_rows + row_off + q * 32 + lane;
+    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+    const bool lce = p.epi >= NL_EPI_LCE_STATS;
+    int t = -1;
+    float lse2 = 0.f, gsc = 0.f, m = -INFINITY, ssum = 0.f, tl = 0.f;
+    if (lce && row < p.M) {
+      t = p.targets[row] - p.col_offset;
+      if (p.epi == NL_EPI_LCE_GRAD) {
+        lse2 = p.lse[row] * kLog2e;
+        gsc = p.grad_scale * (p.gptr ? *p.gptr : 1.f);
+      }
+    }
+#pragma unroll 1
+    for (int c = half * (BN / 32 / split); c < (half + 1) * (BN / 32 / split); ++c) {
+      const int col0 = nb * BN + c * 32;
+      if (col0 >= p.N) break;  // warp-uniform
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      if (!lce) epi_chunk(p, row, col0, v);
+      else if (p.epi == NL_EPI_LCE_STATS) lce_stats_chunk(p, row, col0, v, m, ssum, tl, t);
+      else lce_grad_chunk(p, row, col0, v, lse2, t, gsc);
+    }
+    if (p.epi == NL_EPI_LCE_STATS && row < p.M) {
+      m *= 0.6931471805599453f;  // base-2 max -> natural units
+      p.part[(long long)(2 * nb + half) * p.M + row] = make_float2(m, ssum);
+      if (split == 1) p.part[(long long)(2 * nb + 1) * p.M + row] = make_float2(-INFINITY, 0.f);
+      const int c0 = nb * BN + half * (BN / split);
+      if (t >= c0 && t < c0 + BN / split && t < p.N) p.tgt_logit[row] = tl;
+    }
+    tc_fence_before();
+    if (remote) mbar_arrive_cluster(acc ? tempty1 : tempty0);
+    else mbar_arrive(reinterpret_cast<uint64_t*>(__cvta_shared_to_generic(acc ? tempty1 : tempty0)));
+    acc ^= 1;
+    if (acc == 0) acc_ph ^= 1;
+  }
+  if (lane == 0) bulk_wait_all();  // stores complete before the CTA retires
+}
+
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX, Params p) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES + kStagingBytes);
   uint64_t* full_bar = bars;                       // [STAGES]
   uint64_t* empty_bar = bars + C::STAGES;          // [STAGES]
   uint64_t* tfull_bar = bars + 2 * C::STAGES;      // [2]
@@ -371,56 +576,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;             // TMEM lane quarter this warp may access
-    // with 8 epilogue warps each takes half of the tile's columns; with 4 the
-    // warps 6..9 idle and warps 2..5 take all columns
-    const int split = p.epi_warps / 4;
-    const int half = (warp - 2) >> 2;
-    int acc = 0;
-    uint32_t acc_ph = 0;
-    for (int u = blockIdx.x; half < split && u < num_units; u += gridDim.x) {
-      int mb, nb, sk;
-      decode_unit(p, u, mb, nb, sk);
-      if (!mbar_wait(&tfull_bar[acc], acc_ph, ab)) break;
-      tc_fence_after();
-      const int row = mb * BM + q * 32 + lane;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      const bool lce = p.epi >= NL_EPI_LCE_STATS;
-      int t = -1;
-      float lse2 = 0.f, gsc = 0.f, m = -INFINITY, ssum = 0.f, tl = 0.f;
-      if (lce && row < p.M) {
-        t = p.targets[row] - p.col_offset;
-        if (p.epi == NL_EPI_LCE_GRAD) {
-          lse2 = p.lse[row] * kLog2e;
-          gsc = p.grad_scale * (p.gptr ? *p.gptr : 1.f);
-        }
-      }
-#pragma unroll 1
-      for (int c = half * (BN / 32 / split); c < (half + 1) * (BN / 32 / split); ++c) {
-        const int col0 = nb * BN + c * 32;
-        if (col0 >= p.N) break;  // warp-uniform
-        uint32_t r[32];
-        tmem_ld32(taddr + c * 32, r);
-        tmem_wait_ld();
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        if (!lce) epi_chunk(p, row, col0, v);
-        else if (p.epi == NL_EPI_LCE_STATS) lce_stats_chunk(p, row, col0, v, m, ssum, tl, t);
-        else lce_grad_chunk(p, row, col0, v, lse2, t, gsc);
-      }
-      if (p.epi == NL_EPI_LCE_STATS && row < p.M) {
-        m *= 0.6931471805599453f;  // base-2 max -> natural units
-        p.part[(long long)(2 * nb + half) * p.M + row] = make_float2(m, ssum);
-        if (split == 1) p.part[(long long)(2 * nb + 1) * p.M + row] = make_float2(-INFINITY, 0.f);
-        const int c0 = nb * BN + half * (BN / split);
-        if (t >= c0 && t < c0 + BN / split && t < p.N) p.tgt_logit[row] = tl;
-      }
-      tc_fence_before();
-      mbar_arrive(&tempty_bar[acc]);
-      acc ^= 1;
-      if (acc == 0) acc_ph ^= 1;
-    }
+    epilogue_role<BN>(p, tmem_base, tfull_bar, smem_u32(tempty_bar), smem_u32(tempty_bar + 1), false, BM, 0, ab,
+                      &tmC, &tmX, tiles + C::STAGES * C::STAGE_BYTES);
   }
 
   __syncwarp();
@@ -431,7 +588,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int BN, bool A_MN, bool B_MN>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, Params& p, cudaStream_t stream) {
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& tx, Params& p,
+           cudaStream_t stream) {
   using C = Cfg<BN>;
   auto kern = gemm_kernel<BN, A_MN, B_MN>;
   static int configured_dev = -1;
@@ -444,7 +602,196 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, Params& p, cudaStream_t
   }
   const int units = p.tiles_m * p.tiles_n * p.split_k;
   const int grid = units < sm_count() ? units : sm_count();
-  kern<<<grid, kThreads, C::SMEM, stream>>>(ta, tb, p);
+  kern<<<grid, kThreads, C::SMEM, stream>>>(ta, tb, tc, tx, p);
+  return launch_status();
+}
+
+
+// ============================================================== CTA-pair GEMM
+// Same roles as gemm_kernel, but a 2-CTA cluster computes 256 x 256 tiles with
+// cta_group::2 MMAs (M=256, N=256, K=16) issued by the even CTA.  Each CTA
+// loads its 128 rows of A and its 128 columns of B per k-block (32 KB, 6
+// stages) and holds the accumulator rows of its own half in its TMEM; every
+// load's bytes are counted on the leader's full barrier, and the leader's
+// commits arrive on both CTAs' empty / tfull barriers.  Per FLOP this moves
+// half the B bytes of the single-CTA 128 x 256 tile through L2.
+namespace pair {
+constexpr int BM2 = 256, BN2 = 256;
+constexpr int A_BYTES = 128 * BK * 2;  // 16 KB: this CTA's rows
+constexpr int B_BYTES = 128 * BK * 2;  // 16 KB: this CTA's columns
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int STAGES = 6;
+constexpr int TMEM_COLS = 2 * BN2;
+constexpr int SMEM = STAGES * STAGE_BYTES + kStagingBytes + 1024 + 256;
+}  // namespace pair
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX, Params p) {
+  using namespace pair;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + kStagingBytes);
+  uint64_t* full_bar = bars;                    // [STAGES]  (leader's are used)
+  uint64_t* empty_bar = bars + STAGES;          // [STAGES]
+  uint64_t* tfull_bar = bars + 2 * STAGES;      // [2]
+  uint64_t* tempty_bar = bars + 2 * STAGES + 2; // [2]       (leader's are used)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const int num_units = p.tiles_m * p.tiles_n * p.split_k;
+  const int unit0 = static_cast<int>(blockIdx.x >> 1), ustride = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull_bar[i], 1);
+      mbar_init(&tempty_bar[i], 2 * p.epi_warps * 32);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  Abort ab{abort_flag, p.err};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int u = unit0; u < num_units && ok; u += ustride) {
+        int mb, nb, sk;
+        decode_unit(p, u, mb, nb, sk);
+        const int kb0 = sk * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        const int arow = mb * BM2 + static_cast<int>(rank) * 128;
+        const int bcol = nb * BN2 + static_cast<int>(rank) * 128;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[s], ph ^ 1, ab)) { ok = false; break; }
+          uint8_t* sA = tiles + s * STAGE_BYTES;
+          uint8_t* sB = sA + A_BYTES;
+          const uint32_t fb = mapa_shared(smem_u32(&full_bar[s]), 0);
+          if (rank == 0) mbar_expect_tx(&full_bar[s], 2 * STAGE_BYTES);
+          if (!A_MN) {
+            tma_load_2d_pair(&tmA, fb, sA, kb * BK, arow);
+          } else {
+            tma_load_2d_pair(&tmA, fb, sA, arow, kb * BK);
+            tma_load_2d_pair(&tmA, fb, sA + 8192, arow + 64, kb * BK);
+          }
+          if (!B_MN) {
+            tma_load_2d_pair(&tmB, fb, sB, kb * BK, bcol);
+          } else {
+            tma_load_2d_pair(&tmB, fb, sB, bcol, kb * BK);
+            tma_load_2d_pair(&tmB, fb, sB + 8192, bcol + 64, kb * BK);
+          }
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM2, BN2, A_MN ? 1 : 0, B_MN ? 1 : 0);
+      const uint32_t peer_empty0 = mapa_shared(smem_u32(&empty_bar[0]), 1);
+      const uint32_t own_empty0 = mapa_shared(smem_u32(&empty_bar[0]), 0);
+      const uint32_t peer_tfull0 = mapa_shared(smem_u32(&tfull_bar[0]), 1);
+      const uint32_t own_tfull0 = mapa_shared(smem_u32(&tfull_bar[0]), 0);
+      int s = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t acc_ph = 0;
+      bool ok = true;
+      for (int u = unit0; u < num_units && ok; u += ustride) {
+        int mb, nb, sk;
+        decode_unit(p, u, mb, nb, sk);
+        const int kb0 = sk * p.kb_per_split;
+        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+        if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1, ab)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN2;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full_bar[s], ph, ab)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(tiles + s * STAGE_BYTES);
+          const uint32_t b0 = a0 + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sdesc_sw128(a0 + k * 2048, 8192, 1024) : sdesc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b0 + k * 2048, 8192, 1024) : sdesc_sw128(b0 + k * 32, 16, 1024);
+            umma_f16_ss_pair(d_tmem, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit_pair(own_empty0 + s * 8);
+          umma_commit_pair(peer_empty0 + s * 8);
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit_pair(own_tfull0 + acc * 8);
+        umma_commit_pair(peer_tfull0 + acc * 8);
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1;
+      }
+    }
+  } else {
+    epilogue_role<BN2>(p, tmem_base, tfull_bar, mapa_shared(smem_u32(&tempty_bar[0]), 0),
+                       mapa_shared(smem_u32(&tempty_bar[1]), 0), true, BM2, static_cast<int>(rank) * 128, ab, &tmC,
+                       &tmX, tiles + STAGES * STAGE_BYTES);
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal it
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+}
+
+template <bool A_MN, bool B_MN>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& tx,
+                Params& p, cudaStream_t stream) {
+  auto kern = gemm_pair_kernel<A_MN, B_MN>;
+  static int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pair::SMEM) != cudaSuccess)
+      return NL_ERR_LAUNCH;
+    configured_dev = dev;
+  }
+  const int units = p.tiles_m * p.tiles_n * p.split_k;
+  const int pairs = sm_count() / 2;
+  const int g = units < pairs ? units : pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * g);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = pair::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, tx, p) != cudaSuccess) {
+    cudaGetLastError();
+    return NL_ERR_LAUNCH;
+  }
   return launch_status();
 }
 
@@ -491,6 +838,12 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
       ew = (e && atoi(e) == 4) ? 4 : 8;
     }
     p.epi_warps = ew;
+    static int grp = -1;
+    if (grp < 0) {
+      const char* e = getenv("NL_GEMM_GROUP");
+      grp = (e && atoi(e) > 0) ? atoi(e) : 16;
+    }
+    p.group_m = grp;
   }
   if (ex) {
     p.targets = ex->targets;
@@ -512,14 +865,37 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
     const long long t256 = (long long)((M + BM - 1) / BM) * ((N + 255) / 256);
     if (N <= 128 || t256 < sms) BN = 128;
     if (ex && ex->force_bn) BN = ex->force_bn;
+    static int fbn = -1;
+    if (fbn < 0) {
+      const char* e = getenv("NL_GEMM_FORCE_BN");
+      fbn = e ? atoi(e) : 0;
+    }
+    if (fbn == 128 || fbn == 256) BN = fbn;
   }
-  p.tiles_m = (M + BM - 1) / BM;
+  // 256 x 256 tiles on CTA pairs wherever 256-wide tiles are chosen and there
+  // are enough of them (or a long K to split); NL_GEMM_PAIR=0 disables, 2 forces.
+  static int pair_enabled = -1;
+  if (pair_enabled < 0) {
+    const char* e = getenv("NL_GEMM_PAIR");
+    pair_enabled = e ? atoi(e) : 1;  // 0 off, 1 auto, 2 always (256-wide tiles)
+  }
+  // (measured: pairs win from K >= 1024; at K = 512 the single-CTA kernel is faster)
+  bool use_pair = pair_enabled == 1 ? (BN == 256 && p.num_kb >= 16) : (pair_enabled == 2 && BN == 256);
+  const int workers = use_pair ? sms / 2 : sms;
+  const int unit_m = use_pair ? pair::BM2 : BM;
+  if (use_pair) {
+    const long long t2 = (long long)((M + 255) / 256) * ((N + 255) / 256);
+    if (t2 < workers && !(epi == NL_EPI_ACCUM && p.num_kb >= 16)) use_pair = false;
+  }
+  const int wk = use_pair ? workers : sms;
+  const int um = use_pair ? unit_m : BM;
+  p.tiles_m = (M + um - 1) / um;
   p.tiles_n = (N + BN - 1) / BN;
   const int tiles = p.tiles_m * p.tiles_n;
   // Split-K only for accumulate-mode GEMMs with few tiles and a long K.
   p.split_k = 1;
-  if (epi == NL_EPI_ACCUM && tiles * 2 <= sms && p.num_kb >= 16) {
-    int s = sms / tiles;
+  if (epi == NL_EPI_ACCUM && tiles * 2 <= wk && p.num_kb >= 16) {
+    int s = wk / tiles;
     s = s < p.num_kb / 8 ? s : p.num_kb / 8;
     if (s < 1) s = 1;
     p.split_k = s;
@@ -532,20 +908,36 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
   if (!a_mn) st = make_tmap_bf16_2d(&ta, A, K, M, lda, 64, BM);
   else st = make_tmap_bf16_2d(&ta, A, M, K, lda, 64, BK);
   if (st) return st;
-  if (!b_mn) st = make_tmap_bf16_2d(&tb, B, K, N, ldb, 64, BN);
+  if (!b_mn) st = make_tmap_bf16_2d(&tb, B, K, N, ldb, 64, use_pair ? 128 : BN);
   else st = make_tmap_bf16_2d(&tb, B, N, K, ldb, 64, BK);
   if (st) return st;
-
-  if (BN == 256) {
-    if (!a_mn && !b_mn) return launch<256, false, false>(ta, tb, p, stream);
-    if (!a_mn && b_mn) return launch<256, false, true>(ta, tb, p, stream);
-    if (a_mn && !b_mn) return launch<256, true, false>(ta, tb, p, stream);
-    return launch<256, true, true>(ta, tb, p, stream);
+  // Output through staged TMA stores when the output rows are 16-byte aligned.
+  CUtensorMap tc, tx;
+  memset(&tc, 0, sizeof(tc));
+  memset(&tx, 0, sizeof(tx));
+  p.tma_out = 0;
+  if (Cp != nullptr && epi != NL_EPI_LCE_STATS) {
+    bool ok = make_tmap_out_2d(&tc, Cp, p.c_bf16 != 0, N, M, ldc) == NL_OK;
+    if (ok && epi == NL_EPI_BIAS_GELU) ok = make_tmap_out_2d(&tx, aux, true, N, M, ldc) == NL_OK;
+    p.tma_out = ok ? 1 : 0;
   }
-  if (!a_mn && !b_mn) return launch<128, false, false>(ta, tb, p, stream);
-  if (!a_mn && b_mn) return launch<128, false, true>(ta, tb, p, stream);
-  if (a_mn && !b_mn) return launch<128, true, false>(ta, tb, p, stream);
-  return launch<128, true, true>(ta, tb, p, stream);
+
+  if (use_pair) {
+    if (!a_mn && !b_mn) return launch_pair<false, false>(ta, tb, tc, tx, p, stream);
+    if (!a_mn && b_mn) return launch_pair<false, true>(ta, tb, tc, tx, p, stream);
+    if (a_mn && !b_mn) return launch_pair<true, false>(ta, tb, tc, tx, p, stream);
+    return launch_pair<true, true>(ta, tb, tc, tx, p, stream);
+  }
+  if (BN == 256) {
+    if (!a_mn && !b_mn) return launch<256, false, false>(ta, tb, tc, tx, p, stream);
+    if (!a_mn && b_mn) return launch<256, false, true>(ta, tb, tc, tx, p, stream);
+    if (a_mn && !b_mn) return launch<256, true, false>(ta, tb, tc, tx, p, stream);
+    return launch<256, true, true>(ta, tb, tc, tx, p, stream);
+  }
+  if (!a_mn && !b_mn) return launch<128, false, false>(ta, tb, tc, tx, p, stream);
+  if (!a_mn && b_mn) return launch<128, false, true>(ta, tb, tc, tx, p, stream);
+  if (a_mn && !b_mn) return launch<128, true, false>(ta, tb, tc, tx, p, stream);
+  return launch<128, true, true>(ta, tb, tc, tx, p, stream);
 }
 
 }  // namespace nl

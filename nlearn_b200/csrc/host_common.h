@@ -40,6 +40,25 @@ inline int make_tmap_bf16_2d(CUtensorMap* m, const void* base, uint64_t cols, ui
   return r == CUDA_SUCCESS ? NL_OK : NL_ERR_CUDA;
 }
 
+// Output tile map for the GEMM epilogue's TMA stores: row-major [rows, cols]
+// of f32 (128-byte swizzle) or bf16 (64-byte swizzle), boxes of 32 x 32.
+inline int make_tmap_out_2d(CUtensorMap* m, const void* base, bool bf16, uint64_t cols, uint64_t rows,
+                            uint64_t ld) {
+  auto fn = encode_tiled_fn();
+  if (!fn) return NL_ERR_CUDA;
+  const uint64_t es = bf16 ? 2 : 4;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * es) & 15)) return NL_ERR_ALIGN;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * es};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  bf16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NL_OK : NL_ERR_CUDA;
+}
+
 // Batched row-major bf16 tensor [batch, rows, cols] (contiguous), boxes of
 // box_cols x box_rows x 1 with 128-byte swizzle.  Rows past `rows` of one
 // batch entry read as zero instead of spilling into the next entry.
