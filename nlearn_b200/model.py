@@ -194,7 +194,9 @@ class GPT:
     # ------------------------------------------------------------------ backward
     def backward(self, saved, grad_scale: torch.Tensor | None = None, on_grad_ready=None):
         """Accumulates d(mean loss) into P.grad.  ``on_grad_ready(name)`` is
-        called as each parameter's gradient becomes final (bucket trigger)."""
+        called once a parameter's gradient is final AND the backward has made
+        its last read of that parameter, so the callee may reduce the gradient
+        and update the weight in place (bucket trigger)."""
         cfg, P = self.cfg, self.P
         B, S = saved["B"], saved["S"]
         M, D, H, F, V = B * S, cfg.d_model, cfg.n_heads, cfg.d_ff, cfg.vocab
@@ -220,20 +222,20 @@ class GPT:
             # x3 = x2 + u @ W2 + b2
             gemm_ex(sv["u"], dres_bf, a_trans=True, out=P.g(pre + "w2"), epilogue=_lib.EPI_ACCUM)
             check(lib.nl_colsum_bf16(ptr(dres_bf), ptr(P.g(pre + "b2")), M, D, stream_handle()), "colsum")
-            notify(pre + "w2"); notify(pre + "b2")
             da = gemm_ex(dres_bf, P.p(pre + "w2"), b_trans=True, out_dtype=torch.bfloat16,
                          epilogue=_lib.EPI_DGELU, aux=sv["a"])           # d(pre-activation)
+            notify(pre + "w2"); notify(pre + "b2")   # (after the last read of W2)
             gemm_ex(sv["h2"], da, a_trans=True, out=P.g(pre + "w1"), epilogue=_lib.EPI_ACCUM)
             check(lib.nl_colsum_bf16(ptr(da), ptr(P.g(pre + "b1")), M, F, stream_handle()), "colsum")
-            notify(pre + "w1"); notify(pre + "b1")
             dh2 = gemm_ex(da, P.p(pre + "w1"), b_trans=True, out_dtype=torch.bfloat16)
+            notify(pre + "w1"); notify(pre + "b1")
             _ln_bwd(dh2, sv["x2"], sv["m2"], sv["r2"], P.f(pre + "ln2.g"), dres, dres_bf, P.g(pre + "ln2.g"),
                     P.g(pre + "ln2.b"), M, D, accumulate=True)
             notify(pre + "ln2.g"); notify(pre + "ln2.b")
             # x2 = x + o @ Wo
             gemm_ex(sv["o"], dres_bf, a_trans=True, out=P.g(pre + "wo"), epilogue=_lib.EPI_ACCUM)
-            notify(pre + "wo")
             do = gemm_ex(dres_bf, P.p(pre + "wo"), b_trans=True, out_dtype=torch.bfloat16)
+            notify(pre + "wo")
             dqkv = torch.empty(M, 3 * D, device=dev, dtype=torch.bfloat16)
             Dws = torch.empty(B * H, S, device=dev, dtype=torch.float32)
             acc = torch.empty(B * H, S, 64, device=dev, dtype=torch.float32)
@@ -243,8 +245,8 @@ class GPT:
                                                      ptr(dqkv), ptr(dqkv[:, D:]), ptr(dqkv[:, 2 * D:]), ptr(acc),
                                                      B, H, S, 64, stream_handle()), "attn bwd")
             gemm_ex(sv["h1"], dqkv, a_trans=True, out=P.g(pre + "wqkv"), epilogue=_lib.EPI_ACCUM)
-            notify(pre + "wqkv")
             dh1 = gemm_ex(dqkv, P.p(pre + "wqkv"), b_trans=True, out_dtype=torch.bfloat16)
+            notify(pre + "wqkv")
             _ln_bwd(dh1, sv["x"], sv["m1"], sv["r1"], P.f(pre + "ln1.g"), dres, dres_bf, P.g(pre + "ln1.g"),
                     P.g(pre + "ln1.b"), M, D, accumulate=True)
             notify(pre + "ln1.g"); notify(pre + "ln1.b")
@@ -286,7 +288,13 @@ class AdamW:
         self.hyper.copy_(h, non_blocking=True)
 
     def step(self):
+        self.step_range(0, self.P.numel)
+
+    def step_range(self, start: int, end: int):
+        """AdamW on elements [start, end) of the flat buffers (start, end
+        multiples of 4), on the current stream."""
         P = self.P
-        check(lib.nl_adamw_step(ptr(P.master), ptr(P.grad), ptr(P.exp_avg), ptr(P.exp_avg_sq), ptr(P.shadow),
-                                P.numel, ptr(self.hyper), self.b1, self.b2, self.eps, self.wd, stream_handle()),
-              "nl_adamw_step")
+        n = end - start
+        check(lib.nl_adamw_step(ptr(P.master[start:]), ptr(P.grad[start:]), ptr(P.exp_avg[start:]),
+                                ptr(P.exp_avg_sq[start:]), ptr(P.shadow[start:]), n, ptr(self.hyper), self.b1,
+                                self.b2, self.eps, self.wd, stream_handle()), "nl_adamw_step")

@@ -63,8 +63,9 @@ class BucketReducer:
     every parameter in it final.  Parameters are laid out in gradient-
     production order, so buckets complete front to back."""
 
-    def __init__(self, params: FlatParams, bucket_bytes: int = 64 << 20, group=None):
+    def __init__(self, params: FlatParams, bucket_bytes: int = 64 << 20, group=None, optimizer=None):
         self.P = params
+        self.optimizer = optimizer  # if set, each bucket's AdamW runs right after its all-reduce
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.use_avg = dist.is_initialized() and dist.get_backend(group) == "nccl"
@@ -110,8 +111,12 @@ class BucketReducer:
             self.stream.wait_event(ev)
             with torch.cuda.stream(self.stream):
                 self._allreduce(buf)
+                if self.optimizer is not None:
+                    self.optimizer.step_range(start, end)
         else:
             self._allreduce(buf)
+            if self.optimizer is not None:
+                self.optimizer.step_range(start, end)
         self._launched.append(i)
 
     def _allreduce(self, buf):
@@ -152,7 +157,10 @@ class Trainer:
         self.P = FlatParams(cfg, self.device, seed=tcfg.seed)   # same init on every rank
         self.model = GPT(cfg, self.P)
         self.opt = AdamW(self.P, weight_decay=tcfg.weight_decay)
-        self.reducer = BucketReducer(self.P, tcfg.bucket_mb << 20, group)
+        # with more than one rank the optimizer runs per bucket, overlapped with
+        # the remaining backward, right after that bucket's all-reduce
+        self.reducer = BucketReducer(self.P, tcfg.bucket_mb << 20, group,
+                                     optimizer=self.opt if world > 1 else None)
         self.loader = ZipfLoader(tcfg.batch, tcfg.seq, cfg.vocab, tcfg.seed, rank)
         self.step_idx = 0
         self.warmup = min(tcfg.warmup, tcfg.steps // 5)
@@ -169,12 +177,13 @@ class Trainer:
         """One optimizer step on device-resident tokens; returns the loss tensor
         (not synchronised)."""
         self.P.grad.zero_()
+        self.opt.set_lr(self.lr(self.step_idx))
         loss, saved = self.model.forward(tok, tgt)
         self.reducer.begin()
         self.model.backward(saved, on_grad_ready=self.reducer.ready)
         self.reducer.finish()
-        self.opt.set_lr(self.lr(self.step_idx))
-        self.opt.step()
+        if self.reducer.optimizer is None:
+            self.opt.step()
         self.step_idx += 1
         return loss
 
