@@ -21,7 +21,7 @@
 namespace nl {
 namespace ce {
 
-constexpr int kThreads = 512;
+
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -73,7 +73,7 @@ template <typename T>
 struct Vec { static constexpr int N = 16 / sizeof(T); };
 
 // Row statistics (max, sum-exp) over row[0, V) in base-2 units.
-template <typename T>
+template <int kThreads, typename T>
 __device__ Stat row_stat(const T* row, int V) {
   constexpr int VN = Vec<T>::N;
   Stat st{-INFINITY, 0.f};
@@ -123,7 +123,7 @@ __device__ Stat row_stat(const T* row, int V) {
 }
 
 // dlogits[v] = (2^(x log2e - lse2) - [v == t]) * scale
-template <typename T, typename TO>
+template <int kThreads, typename T, typename TO>
 __device__ void row_grad(const T* row, TO* drow, int V, int t, float lse2, float scale) {
   for (int i = threadIdx.x; i < V; i += kThreads) {
     // scalar path keeps any leading dimension legal; rows are L2-resident here
@@ -132,7 +132,7 @@ __device__ void row_grad(const T* row, TO* drow, int V, int t, float lse2, float
   }
 }
 
-template <typename T, typename TO>
+template <int kThreads, typename T, typename TO>
 __device__ void row_grad_vec(const T* row, TO* drow, int V, int t, float lse2, float scale) {
   // vector path when row and drow share 16-byte phase and element size
   constexpr int VN = Vec<T>::N;
@@ -173,7 +173,7 @@ __device__ void row_grad_vec(const T* row, TO* drow, int V, int t, float lse2, f
 }
 
 // mode: 1 = fwd (loss, lse), 2 = bwd (dlogits from given lse), 3 = fused fwd+bwd
-template <typename T, typename TO, int MODE>
+template <typename T, typename TO, int MODE, int kThreads>
 __global__ void __launch_bounds__(kThreads) ce_kernel(const T* logits, long long ld,
                                                       const int* __restrict__ targets, float* loss, float* lse,
                                                       TO* dlogits, long long ldd, int M, int V, float scale) {
@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(kThreads) ce_kernel(const T* logits, long long
   const float xt = (threadIdx.x == 0 && tin) ? ld1(row + t) : 0.f;
   float lse2;
   if (MODE & 1) {
-    const Stat st = row_stat(row, V);
+    const Stat st = row_stat<kThreads>(row, V);
     lse2 = st.m + __log2f(st.s);
     if (threadIdx.x == 0) {
       const float l = lse2 * kLn2;
@@ -201,8 +201,8 @@ __global__ void __launch_bounds__(kThreads) ce_kernel(const T* logits, long long
     TO* drow = dlogits + (long long)r * ldd;
     const bool same_phase = sizeof(T) == sizeof(TO) &&
                             ((reinterpret_cast<uintptr_t>(row) & 15) == (reinterpret_cast<uintptr_t>(drow) & 15));
-    if (same_phase) row_grad_vec<T, TO>(row, drow, V, tin ? t : -1, lse2, scale);
-    else row_grad<T, TO>(row, drow, V, tin ? t : -1, lse2, scale);
+    if (same_phase) row_grad_vec<kThreads, T, TO>(row, drow, V, tin ? t : -1, lse2, scale);
+    else row_grad<kThreads, T, TO>(row, drow, V, tin ? t : -1, lse2, scale);
   }
 }
 
@@ -212,10 +212,15 @@ int dispatch(const void* logits, long long ld, int in_dtype, const int* targets,
   if (M <= 0 || V <= 0 || ld < V || ((MODE & 2) && ldd < V)) return NL_ERR_SHAPE;
   if (in_dtype != NL_F32 && in_dtype != NL_BF16) return NL_ERR_DTYPE;
   if ((MODE & 2) && out_dtype != NL_F32 && out_dtype != NL_BF16) return NL_ERR_DTYPE;
-  dim3 grid(M), block(kThreads);
-#define NL_CE_LAUNCH(T, TO)                                                                                  \
-  ce_kernel<T, TO, MODE><<<grid, block, 0, stream>>>(reinterpret_cast<const T*>(logits), ld, targets, loss, lse, \
-                                                     reinterpret_cast<TO*>(dlogits), ldd, M, V, scale)
+  // The fused form re-reads each row from L2 in its second pass: with one
+  // 1024-thread CTA per SM only ~148 rows are in flight, which keeps them
+  // L2-resident (a 50k-column f32 row is 200 KB); single-pass forms use
+  // 512-thread CTAs, several per SM.
+  constexpr int NT = (MODE == 3) ? 1024 : 512;
+  dim3 grid(M), block(NT);
+#define NL_CE_LAUNCH(T, TO)                                                                                    \
+  ce_kernel<T, TO, MODE, NT><<<grid, block, 0, stream>>>(reinterpret_cast<const T*>(logits), ld, targets, loss, \
+                                                         lse, reinterpret_cast<TO*>(dlogits), ldd, M, V, scale)
   if (in_dtype == NL_F32) {
     if (!(MODE & 2) || out_dtype == NL_F32) NL_CE_LAUNCH(float, float);
     else NL_CE_LAUNCH(float, __nv_bfloat16);

@@ -21,7 +21,7 @@
 // Causal tiles above the diagonal are never visited; heavy (late) query tiles
 // are scheduled first.
 //
-// Backward, one CTA per (head, 128-key tile), 10 warps, 1 CTA per SM:
+// Backward, one CTA per (head, 128-key tile), 14 warps, 1 CTA per SM:
 //   warp 0     TMA: K, V once; Q_i / dO_i into 2-slot rings
 //   warp 1     TMEM alloc (512 cols) + MMA issuer, per query tile i >= key tile:
 //                S^T  = K Q_i^T        cols [0,128)
@@ -29,9 +29,10 @@
 //                dV  += P^T dO_i       cols [256,320)   (B = dO_i read MN-major)
 //                dK  += dS^T Q_i       cols [320,384)   (B = Q_i  read MN-major)
 //                dQ_i = dS K           cols [384,448)   (A = dS^T read MN-major)
-//   warps 2-5  one key row per thread: P^T = exp2(S^T scale log2e - L log2e),
+//   warps 2-9  one key row per thread, two warps per row quarter splitting the
+//              query columns: P^T = exp2(S^T scale log2e - L log2e),
 //              dS^T = P^T (dP^T - D); both -> bf16 shared memory
-//   warps 6-9  dQ_i tile: TMEM -> float4 atomics into an f32 accumulator
+//   warps 10-13 dQ_i tile: TMEM -> float4 atomics into an f32 accumulator
 // followed by a convert kernel dQ = bf16(scale * dQacc).
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -299,7 +300,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
 
 // ====================================================================== backward
 namespace bwd {
-constexpr int kThreads = 10 * 32;
+constexpr int kThreads = 14 * 32;  // TMA, MMA, 8 P/dS warps, 4 dQ warps
 constexpr int OFF_K = 0;
 constexpr int OFF_V = TILE;
 constexpr int OFF_Q = 2 * TILE;   // 2 slots
@@ -365,8 +366,8 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       mbar_init(&qdo_empty[i], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(st_free, 128);
-    mbar_init(ds_full, 128);
+    mbar_init(st_free, 256);
+    mbar_init(ds_full, 256);
     mbar_init(ds_empty, 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 128);
@@ -448,11 +449,14 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       }
       if (ok) umma_commit(acc_done);
     }
-  } else if (warp < 6) {
-    // ---------------------------------------------------------- P / dS warps (one key row each)
+  } else if (warp < 10) {
+    // ---------------------------------------------------------- P / dS warps
+    // two warps per TMEM lane quarter (one key row per thread), each taking
+    // half of the 128 query columns
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
-    const int t = (warp - 2) * 32 + lane;  // 0..127 loader index
+    const int t = (warp - 2) * 32 + lane;  // loader index: threads 0..127 stage L / D
     const int kv = jb * BKV + r;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const uint32_t sP = smem_u32(smem + OFF_P), sDS = smem_u32(smem + OFF_DS);
@@ -461,21 +465,23 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     float l_next, d_next;
     {
       const int qi = jb * BQ + t;
-      l_next = (qi < p.s) ? Lh[qi] * kLog2e : INFINITY;
-      d_next = (qi < p.s) ? Dh[qi] : 0.f;
+      l_next = (t < 128 && qi < p.s) ? Lh[qi] * kLog2e : INFINITY;
+      d_next = (t < 128 && qi < p.s) ? Dh[qi] : 0.f;
     }
-    // On a timeout the loop keeps iterating without work so that all 128
+    // On a timeout the loop keeps iterating without work so that all 256
     // threads still meet at every named barrier (a barrier can not time out).
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
       const int i = jb + it, buf = it & 1;
-      Lbuf[buf * 128 + t] = l_next;
-      Dbuf[buf * 128 + t] = d_next;
-      named_bar_sync(1, 128);
+      if (t < 128) {
+        Lbuf[buf * 128 + t] = l_next;
+        Dbuf[buf * 128 + t] = d_next;
+      }
+      named_bar_sync(1, 256);
       if (it + 1 < n_it) {
         const int qi = (i + 1) * BQ + t;
-        l_next = (qi < p.s) ? Lh[qi] * kLog2e : INFINITY;
-        d_next = (qi < p.s) ? Dh[qi] : 0.f;
+        l_next = (t < 128 && qi < p.s) ? Lh[qi] * kLog2e : INFINITY;
+        d_next = (t < 128 && qi < p.s) ? Dh[qi] : 0.f;
       }
       if (ok) ok = mbar_wait_warp(s_full, it & 1, ab);
       if (ok && it > 0) ok = mbar_wait_warp(ds_empty, (it - 1) & 1, ab);
@@ -484,7 +490,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       const float* Lb = Lbuf + buf * 128;
       const float* Db = Dbuf + buf * 128;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 2 * half; c < 2 * half + 2; ++c) {
         uint32_t us[32], ud[32];
         tmem_ld32(trow + COL_S + c * 32, us);
         tmem_ld32(trow + COL_DP + c * 32, ud);
@@ -519,8 +525,8 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     }
     if (ok && p.want_dkdv && mbar_wait_warp(acc_done, 0, ab)) {
       tc_fence_after();
-#pragma unroll
-      for (int which = 0; which < 2; ++which) {
+      {
+        const int which = half;  // half 0 writes dV, half 1 writes dK
         __nv_bfloat16* dst = (which == 0 ? p.dV : p.dK) + bi * p.gs.b + (long long)kv * p.gs.s + hi * p.gs.h;
         const float mul = (which == 0) ? 1.f : p.scale;
         const uint32_t col = (which == 0) ? COL_DV : COL_DK;
@@ -580,38 +586,60 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
 }
 
 // D[row] = sum_d dO[row,d] * O[row,d]; optionally zero the dQ accumulator row.
-// One warp per row (64 bf16 = 32 bf16x2).
+// Eight threads per row (16-byte loads of 8 bf16 each), four rows per warp,
+// grid-stride so that each thread keeps several independent loads in flight.
 __global__ void bwd_preprocess_kernel(const __nv_bfloat16* __restrict__ O, const __nv_bfloat16* __restrict__ dO,
                                       Strides os, int H, int s, float* __restrict__ D, float* __restrict__ dQacc,
                                       long long rows) {
-  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  float acc = 0.f;
-  if (O != nullptr) {
-    const long long nh = row / s, q = row % s;
-    const long long off = (nh / H) * os.b + q * os.s + (nh % H) * os.h;
-    const __nv_bfloat162 o = reinterpret_cast<const __nv_bfloat162*>(O + off)[lane];
-    const __nv_bfloat162 g = reinterpret_cast<const __nv_bfloat162*>(dO + off)[lane];
-    const float2 of = __bfloat1622float2(o), gf = __bfloat1622float2(g);
-    acc = of.x * gf.x + of.y * gf.y;
+  const int sub = threadIdx.x & 7;
+  for (long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 3; row < rows;
+       row += (static_cast<long long>(gridDim.x) * blockDim.x) >> 3) {
+    if (O != nullptr) {
+      const long long nh = row / s, q = row % s;
+      const long long off = (nh / H) * os.b + q * os.s + (nh % H) * os.h + sub * 8;
+      const uint4 o = *reinterpret_cast<const uint4*>(O + off);
+      const uint4 g = *reinterpret_cast<const uint4*>(dO + off);
+      const __nv_bfloat162* oh = reinterpret_cast<const __nv_bfloat162*>(&o);
+      const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&g);
+      float acc = 0.f;
 #pragma unroll
-    for (int o2 = 16; o2 > 0; o2 >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o2);
-    if (lane == 0) D[row] = acc;
+      for (int k = 0; k < 4; ++k) {
+        const float2 a = __bfloat1622float2(oh[k]), b = __bfloat1622float2(gh[k]);
+        acc += a.x * b.x + a.y * b.y;
+      }
+      acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      if (sub == 0) D[row] = acc;
+    }
+    if (dQacc) {
+      float4* z = reinterpret_cast<float4*>(dQacc + row * HD) + sub * 2;
+      z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
-  if (dQacc) reinterpret_cast<float2*>(dQacc + row * HD)[lane] = make_float2(0.f, 0.f);
 }
 
+// dQ = bf16(scale * dQacc): 8 elements per thread, 16-byte stores into the
+// (possibly strided) dQ layout.
 __global__ void dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dQ, Strides gs, int H,
-                                  int s, float scale, long long n4) {
-  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= n4) return;
-  const long long row = i >> 4, c4 = i & 15;
-  const long long nh = row / s, q = row % s;
-  const long long off = (nh / H) * gs.b + q * gs.s + (nh % H) * gs.h + c4 * 4;
-  const float4 v = reinterpret_cast<const float4*>(acc)[i];
-  *reinterpret_cast<uint2*>(dQ + off) =
-      make_uint2(pack_bf16x2(v.x * scale, v.y * scale), pack_bf16x2(v.z * scale, v.w * scale));
+                                  int s, float scale, long long n8) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = i >> 3, c8 = i & 7;
+    const long long nh = row / s, q = row % s;
+    const long long off = (nh / H) * gs.b + q * gs.s + (nh % H) * gs.h + c8 * 8;
+    const float4 a = reinterpret_cast<const float4*>(acc)[2 * i];
+    const float4 b = reinterpret_cast<const float4*>(acc)[2 * i + 1];
+    *reinterpret_cast<uint4*>(dQ + off) =
+        make_uint4(pack_bf16x2(a.x * scale, a.y * scale), pack_bf16x2(a.z * scale, a.w * scale),
+                   pack_bf16x2(b.x * scale, b.y * scale), pack_bf16x2(b.z * scale, b.w * scale));
+  }
+}
+
+static int grid_cap(long long blocks) {
+  const long long cap = static_cast<long long>(sm_count()) * 16;
+  return static_cast<int>(blocks < cap ? blocks : cap);
 }
 
 static int check_common(const void* Q, const void* K, const void* V, int n, int s, int d) {
@@ -687,8 +715,8 @@ int flash_bwd(const void* Q, const void* K, const void* V, fa::Strides qs, const
     return NL_ERR_ALIGN;
   const long long rows = static_cast<long long>(n) * s;
   if (O || want_dq) {
-    const long long threads = rows * 32;
-    bwd_preprocess_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
+    const long long threads = rows * 8;
+    bwd_preprocess_kernel<<<grid_cap((threads + 255) / 256), 256, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(O), reinterpret_cast<const __nv_bfloat16*>(dO), os, H, s, D,
         want_dq ? dQacc : nullptr, rows);
     if ((st = launch_status())) return st;
@@ -719,9 +747,9 @@ int flash_bwd(const void* Q, const void* K, const void* V, fa::Strides qs, const
   flash_bwd_kernel<<<static_cast<unsigned>(grid), bwd::kThreads, bwd::SMEM, stream>>>(tq, tk, tv, tdo, p);
   if ((st = launch_status())) return st;
   if (want_dq) {
-    const long long n4 = rows * HD / 4;
-    dq_convert_kernel<<<static_cast<unsigned>((n4 + 255) / 256), 256, 0, stream>>>(
-        dQacc, reinterpret_cast<__nv_bfloat16*>(dQ), qs, H, s, p.scale, n4);
+    const long long n8 = rows * HD / 8;
+    dq_convert_kernel<<<grid_cap((n8 + 255) / 256), 256, 0, stream>>>(
+        dQacc, reinterpret_cast<__nv_bfloat16*>(dQ), qs, H, s, p.scale, n8);
     if ((st = launch_status())) return st;
   }
   return NL_OK;
