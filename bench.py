@@ -271,11 +271,14 @@ def main():
     flash = flash_op_tflops(dev) if rank == 0 else None
     burst, sustained, hbm, src = peaks()
     achieved = HEAD_GEMM_FLOP / (head_avg_ms * 1e-3) / 1e12
+    # DRAM bytes per launch of the same kernel, from the committed ncu summary
     traffic = None
-    tf = os.path.join(ROOT, "profiles", "traffic.json")
+    tf = os.path.join(ROOT, "profiles", "gemm_lce_head_fwd_M4096.md")
     if os.path.exists(tf):
+        import re
         with open(tf) as f:
-            traffic = json.load(f).get("lce_head_gemm_bytes_per_launch")
+            mt = re.search(r"lce_head_gemm_bytes_per_launch\s*=\s*(\d+)", f.read())
+        traffic = int(mt.group(1)) if mt else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, cores, sample = cpu_step_rate(threads=len(os.sched_getaffinity(0)), batch=1, steps=2)
