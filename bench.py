@@ -174,6 +174,41 @@ def flash_op_tflops(dev, iters=20):
             "tflops": ATTN_FWD_BWD_FLOP / (ms * 1e-3) / 1e12}
 
 
+def long_context(dev, rank, world, steps=5, warmup=3):
+    """the same model at seq 4096, GLOBAL batch 8 split over the
+    ranks (strong scaling; one sequence per rank at 8 GPUs).  Device-timed
+    tokens/s of the whole job, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from nlearn_b200.model import GPTConfig
+    from nlearn_b200.train import Trainer, TrainConfig
+    per_rank = max(1, 8 // world)
+    tr = Trainer(GPTConfig(max_seq=4096), TrainConfig(batch=per_rank, seq=4096, steps=1000, peak_lr=1e-3,
+                                                      warmup=200), dev, rank, world)
+    bat = [tr.device_batch(*tr.loader.next()) for _ in range(warmup + steps)]
+    for i in range(warmup):
+        tr.step_on_device(*bat[i])
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(warmup, warmup + steps):
+        tr.step_on_device(*bat[i])
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t) / steps
+    tokens = per_rank * world * 4096
+    del tr, bat
+    torch.cuda.empty_cache()
+    return {"config": "seq 4096, global batch 8 (configs[4]), strong scaling", "per_rank_batch": per_rank,
+            "ms_per_step": ms, "value": tokens / (ms * 1e-3), "unit": UNIT,
+            "mfu": tokens / (ms * 1e-3) * 280.2e6 / (world * peaks()[1] * 1e12)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -181,6 +216,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-long", action="store_true", help="skip the seq-4096 long-context measurement")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank = int(os.environ.get("RANK", "0"))
@@ -226,12 +262,12 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
+    clocks = ClockSampler(local)
+    clocks.start()  # sampled over warm-up, timed, end-to-end and long-context runs (all under load)
     for i in range(args.warmup):
         tr.step_on_device(*dbat[i])
     head_ms.clear()
     barrier()
-    clocks = ClockSampler(local)
-    clocks.start()
     l0 = _lib.lib.nl_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -241,7 +277,6 @@ def main():
     barrier()
     launches = _lib.lib.nl_launch_count() - l0
     ms = e0.elapsed_time(e1)
-    clk = clocks.stop()
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -269,6 +304,8 @@ def main():
     e2e_value = tokens / (float(t2) * 1e-3)
 
     flash = flash_op_tflops(dev) if rank == 0 else None
+    longc = long_context(dev, rank, world) if not args.no_long else None
+    clk = clocks.stop()
     burst, sustained, hbm, src = peaks()
     achieved = HEAD_GEMM_FLOP / (head_avg_ms * 1e-3) / 1e12
     # DRAM bytes per launch of the same kernel, from the committed ncu summary
@@ -303,6 +340,7 @@ def main():
                          "frac": achieved / sustained, "peak_source": f"{src} bf16_tflops_sustained",
                          "traffic": traffic, "avg_launch_ms": head_avg_ms},
             "flash_attention": flash,
+            "long_context": longc,
             "clocks": clk,
             "cpu_baseline": cpu,
             "final_loss": lv,
