@@ -90,18 +90,30 @@ __global__ void layernorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const 
                                      float* __restrict__ mean_out, float* __restrict__ rstd_out, int M, int D,
                                      float eps) {
   const int lane = threadIdx.x & 31;
+  // each lane always owns the same 8-column groups: keep gamma / beta in registers
+  float gg[DV][8], bb[DV][8];
+#pragma unroll
+  for (int j = 0; j < DV; ++j) {
+    const float4* g4 = reinterpret_cast<const float4*>(g + (lane + 32 * j) * 8);
+    const float4* b4 = reinterpret_cast<const float4*>(b + (lane + 32 * j) * 8);
+    const float4 g0 = __ldg(g4), g1 = __ldg(g4 + 1), b0 = __ldg(b4), b1 = __ldg(b4 + 1);
+    gg[j][0] = g0.x; gg[j][1] = g0.y; gg[j][2] = g0.z; gg[j][3] = g0.w;
+    gg[j][4] = g1.x; gg[j][5] = g1.y; gg[j][6] = g1.z; gg[j][7] = g1.w;
+    bb[j][0] = b0.x; bb[j][1] = b0.y; bb[j][2] = b0.z; bb[j][3] = b0.w;
+    bb[j][4] = b1.x; bb[j][5] = b1.y; bb[j][6] = b1.z; bb[j][7] = b1.w;
+  }
   for (long long m = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; m < M;
        m += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + m * D);
     float v[DV][8];
-    float s = 0.f;
+    float sum = 0.f;
 #pragma unroll
     for (int j = 0; j < DV; ++j) {
       unpack8(xr[lane + 32 * j], v[j]);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) s += v[j][i];
+      for (int i = 0; i < 8; ++i) sum += v[j][i];
     }
-    const float mean = warp_sum(s) / D;
+    const float mean = warp_sum(sum) / D;
     float q = 0.f;
 #pragma unroll
     for (int j = 0; j < DV; ++j)
@@ -114,10 +126,9 @@ __global__ void layernorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const 
     uint4* yr = reinterpret_cast<uint4*>(y + m * D);
 #pragma unroll
     for (int j = 0; j < DV; ++j) {
-      const int c = (lane + 32 * j) * 8;
       float o[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = (v[j][i] - mean) * rstd * __ldg(g + c + i) + __ldg(b + c + i);
+      for (int i = 0; i < 8; ++i) o[i] = (v[j][i] - mean) * rstd * gg[j][i] + bb[j][i];
       yr[lane + 32 * j] = pack8(o);
     }
     if (lane == 0) {
@@ -140,6 +151,14 @@ __global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const
   for (int j = 0; j < DV; ++j)
 #pragma unroll
     for (int i = 0; i < 8; ++i) adg[j][i] = adb[j][i] = 0.f;
+  float gg[DV][8];
+#pragma unroll
+  for (int j = 0; j < DV; ++j) {
+    const float4* g4 = reinterpret_cast<const float4*>(g + (lane + 32 * j) * 8);
+    const float4 g0 = __ldg(g4), g1 = __ldg(g4 + 1);
+    gg[j][0] = g0.x; gg[j][1] = g0.y; gg[j][2] = g0.z; gg[j][3] = g0.w;
+    gg[j][4] = g1.x; gg[j][5] = g1.y; gg[j][6] = g1.z; gg[j][7] = g1.w;
+  }
   for (long long m = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; m < M;
        m += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
     const float mean = mean_in[m], rstd = rstd_in[m];
@@ -152,11 +171,10 @@ __global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const
       float xv[8], dv[8];
       unpack8(xr[lane + 32 * j], xv);
       unpack8(dyr[lane + 32 * j], dv);
-      const int c = (lane + 32 * j) * 8;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         xh[j][i] = (xv[i] - mean) * rstd;
-        gd[j][i] = dv[i] * __ldg(g + c + i);
+        gd[j][i] = dv[i] * gg[j][i];
         s1 += gd[j][i];
         s2 += gd[j][i] * xh[j][i];
         adg[j][i] += dv[i] * xh[j][i];
