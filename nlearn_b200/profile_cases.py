@@ -40,6 +40,7 @@ def main(argv=None):
     ap.add_argument("--layout", default="nn")
     ap.add_argument("--chunk", type=int, default=0)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--pad", type=int, default=0, help="extra elements of row pitch for the GEMM operands")
     a = ap.parse_args(argv)
     dev = torch.device("cuda:0")
     torch.manual_seed(0)
@@ -68,11 +69,13 @@ def main(argv=None):
         from .kernels.gemm import gemm_ex
         M, N, K = a.M, a.N, a.K
         at, bt = a.layout[0] == "t", a.layout[1] == "t"
-        A = torch.randn(*((K, M) if at else (M, K)), device=dev).bfloat16()
-        B = torch.randn(*((N, K) if bt else (K, N)), device=dev).bfloat16()
+        def mk(r, c):  # rows x cols with row pitch c + pad
+            return torch.randn(r, c + a.pad, device=dev).bfloat16()[:, :c]
+        A = mk(*((K, M) if at else (M, K)))
+        B = mk(*((N, K) if bt else (K, N)))
         C = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
         ms = _time(lambda: gemm_ex(A, B, a_trans=at, b_trans=bt, out=C), a.iters)
-        out.update(M=M, N=N, K=K, layout=a.layout, ms=ms, tflops=2 * M * N * K / ms / 1e9)
+        out.update(M=M, N=N, K=K, layout=a.layout, pad=a.pad, ms=ms, tflops=2 * M * N * K / ms / 1e9)
     elif a.case in ("attn_fwd", "attn_bwd"):
         from . import attention as A
         n, s = a.heads, a.seq
