@@ -892,13 +892,22 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
   p.tiles_m = (M + um - 1) / um;
   p.tiles_n = (N + BN - 1) / BN;
   const int tiles = p.tiles_m * p.tiles_n;
-  // Split-K only for accumulate-mode GEMMs with few tiles and a long K.
+  // Split-K for accumulate-mode GEMMs (the splits combine through the TMA
+  // reduce-add): pick the split, at least 8 k-blocks each, that gives the
+  // best wave efficiency units / (waves * workers); ties go to fewer splits.
   p.split_k = 1;
-  if (epi == NL_EPI_ACCUM && tiles * 2 <= wk && p.num_kb >= 16) {
-    int s = wk / tiles;
-    s = s < p.num_kb / 8 ? s : p.num_kb / 8;
-    if (s < 1) s = 1;
-    p.split_k = s;
+  if (epi == NL_EPI_ACCUM && p.num_kb >= 16) {
+    double best = 0.0;
+    const int smax = p.num_kb / 8 < 16 ? p.num_kb / 8 : 16;
+    for (int sk = 1; sk <= smax; ++sk) {
+      const long long units = (long long)tiles * sk;
+      const long long waves = (units + wk - 1) / wk;
+      const double eff = (double)units / (double)(waves * wk);
+      if (eff > best + 0.02) {
+        best = eff;
+        p.split_k = sk;
+      }
+    }
   }
   p.kb_per_split = (p.num_kb + p.split_k - 1) / p.split_k;
   p.split_k = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
