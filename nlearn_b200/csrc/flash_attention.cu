@@ -212,14 +212,14 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
     for (int j = 0; j < nkv; ++j) {
       if (!mbar_wait_warp(s_full, j & 1, ab)) { ok = false; break; }
       tc_fence_after();
-      float sv[128];
+      float sv[128];  // raw scores; the softmax scale is folded into the exponent FFMA
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t u[32];
         tmem_ld32(trow + COL_S + c * 32, u);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) sv[c * 32 + e] = __uint_as_float(u[e]) * p.sl2;
+        for (int e = 0; e < 32; ++e) sv[c * 32 + e] = __uint_as_float(u[e]);
       }
       tc_fence_before();
       mbar_arrive(s_free);
@@ -231,13 +231,17 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
       float mt = sv[0];
 #pragma unroll
       for (int e = 1; e < 128; ++e) mt = fmaxf(mt, sv[e]);
-      const float m_new = fmaxf(m, mt);
+      mt *= p.sl2;  // (scale > 0, so the max commutes with it)
+      // Lazy rescale: keep the running max unless the tile's max exceeds it by
+      // more than 8 (log2 units).  Then P <= 2^8 and O, l stay in f32 range,
+      // and most key tiles after the first skip the O rescale entirely.
+      const float m_new = (mt > m + 8.f) ? mt : m;
       float lt = 0.f;
       uint32_t pk[64];
 #pragma unroll
       for (int e = 0; e < 64; ++e) {
-        const float a = ex2_approx(sv[2 * e] - m_new);
-        const float b = ex2_approx(sv[2 * e + 1] - m_new);
+        const float a = ex2_approx(fmaf(sv[2 * e], p.sl2, -m_new));
+        const float b = ex2_approx(fmaf(sv[2 * e + 1], p.sl2, -m_new));
         lt += a + b;
         pk[e] = pack_bf16x2(a, b);
       }
