@@ -12,12 +12,13 @@
 //   warp 0     TMA: Q once, K_j / V_j into 2-slot rings
 //   warp 1     TMEM alloc (256 cols) + tcgen05.mma issuer:
 //                S = Q K_j^T  -> TMEM cols [0,128)    (M=128, N=128, K=64)
-//                O += P_j V_j -> TMEM cols [128,192)  (M=128, N=64,  K=128)
+//                O += P_j V_j -> TMEM cols [128,192)  (M=128, N=64,  K=128; P read
+//                                from TMEM cols [192,256), V from shared memory)
 //              S_{j+1} is issued as soon as the softmax warps have pulled S_j
 //              into registers, so it overlaps softmax_j.
 //   warps 2-5  softmax, one query row per thread: exp2-domain online softmax,
 //              O rescale in TMEM (tcgen05.ld/st) when the row max grows,
-//              P_j -> bf16 in shared memory in the UMMA K-major SW128 layout.
+//              P_j -> bf16 pairs in TMEM (the A operand of the PV MMA).
 // Causal tiles above the diagonal are never visited; heavy (late) query tiles
 // are scheduled first.
 //
@@ -72,11 +73,10 @@ constexpr int kThreads = 6 * 32;
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = TILE;           // 2 slots
 constexpr int OFF_V = 3 * TILE;       // 2 slots
-constexpr int OFF_P = 5 * TILE;       // 32 KB
-constexpr int OFF_BAR = 7 * TILE;
+constexpr int OFF_BAR = 5 * TILE;
 constexpr int SMEM = OFF_BAR + 256;
 constexpr int TMEM_COLS = 256;
-constexpr int COL_S = 0, COL_O = 128;
+constexpr int COL_S = 0, COL_O = 128, COL_P = 192;  // P: 128 bf16 per row packed in 64 columns
 }  // namespace fwd
 
 // Activations are addressed as [b][h][s][64] with element strides, so Q/K/V
@@ -169,7 +169,6 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
       constexpr uint32_t idS = idesc_bf16_f32(128, 128, 0, 0);
       constexpr uint32_t idO = idesc_bf16_f32(128, 64, 0, 1);
       const uint32_t sQ = smem_u32(smem + OFF_Q);
-      const uint32_t sP = smem_u32(smem + OFF_P);
       bool ok = mbar_wait(q_full, 0, ab);
       for (int j = 0; ok && j <= nkv; ++j) {
         if (j < nkv) {
@@ -192,9 +191,9 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
           tc_fence_after();
           const uint32_t sV = smem_u32(smem + OFF_V + slot * TILE);
 #pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk)
-            umma_f16_ss(tmem + COL_O, sdesc_sw128(sP + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                        sdesc_sw128(sV + kk * 2048, 8192, 1024), idO, (jj > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BKV / 16; ++kk)  // P (A operand) read from TMEM, 8 columns per k-step
+            umma_f16_ts(tmem + COL_O, tmem + COL_P + kk * 8, sdesc_sw128(sV + kk * 2048, 8192, 1024), idO,
+                        (jj > 0 || kk > 0) ? 1u : 0u);
           umma_commit(o_done);
           umma_commit(&v_empty[slot]);
         }
@@ -206,7 +205,6 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
     const int r = quarter * 32 + lane;
     const int q = qb * BQ + r;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    const uint32_t sP = smem_u32(smem + OFF_P);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
@@ -265,10 +263,16 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
       }
       l = l * alpha + lt;
       m = m_new;
+      {  // P (bf16 pairs) into TMEM columns [COL_P, COL_P + 64) of this row's lane
+        uint32_t w[32];
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8)
-        st_shared_v4(sP + sw128_off(r, c8), pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
-      fence_proxy_async_smem();
+        for (int e = 0; e < 32; ++e) w[e] = pk[e];
+        tmem_st32(trow + COL_P, w);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) w[e] = pk[32 + e];
+        tmem_st32(trow + COL_P + 32, w);
+        tmem_wait_st();
+      }
       tc_fence_before();
       mbar_arrive(p_full);
     }
