@@ -27,12 +27,13 @@
 //   warp 1     TMEM alloc (512 cols) + MMA issuer, per query tile i >= key tile:
 //                S^T  = K Q_i^T        cols [0,128)
 //                dP^T = V dO_i^T       cols [128,256)
-//                dV  += P^T dO_i       cols [256,320)   (B = dO_i read MN-major)
+//                dV  += P^T dO_i       cols [256,320)   (A = P^T from TMEM cols [448,512),
+//                                                        B = dO_i read MN-major)
 //                dK  += dS^T Q_i       cols [320,384)   (B = Q_i  read MN-major)
 //                dQ_i = dS K           cols [384,448)   (A = dS^T read MN-major)
 //   warps 2-9  one key row per thread, two warps per row quarter splitting the
 //              query columns: P^T = exp2(S^T scale log2e - L log2e),
-//              dS^T = P^T (dP^T - D); both -> bf16 shared memory
+//              dS^T = P^T (dP^T - D); P^T -> bf16 in TMEM, dS^T -> bf16 shared memory
 //   warps 10-13 dQ_i tile: TMEM -> float4 atomics into an f32 accumulator
 // followed by a convert kernel dQ = bf16(scale * dQacc).
 #include <cuda_runtime.h>
@@ -313,13 +314,13 @@ constexpr int OFF_K = 0;
 constexpr int OFF_V = TILE;
 constexpr int OFF_Q = 2 * TILE;   // 2 slots
 constexpr int OFF_DO = 4 * TILE;  // 2 slots
-constexpr int OFF_P = 6 * TILE;   // 32 KB  P^T  [kv rows, q cols]
-constexpr int OFF_DS = 8 * TILE;  // 32 KB  dS^T [kv rows, q cols]
-constexpr int OFF_LD = 10 * TILE; // L2[2][128], D[2][128] f32
+constexpr int OFF_DS = 6 * TILE;  // 32 KB  dS^T [kv rows, q cols]
+constexpr int OFF_LD = 8 * TILE;  // L2[2][128], D[2][128] f32
 constexpr int OFF_BAR = OFF_LD + 2048;
 constexpr int SMEM = OFF_BAR + 256;
 constexpr int TMEM_COLS = 512;
 constexpr int COL_S = 0, COL_DP = 128, COL_DV = 256, COL_DK = 320, COL_DQ = 384;
+constexpr int COL_PT = 448;  // P^T as bf16 pairs: 128 query columns in 64 TMEM columns
 }  // namespace bwd
 
 struct BwdParams {
@@ -413,7 +414,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       constexpr uint32_t idKV = idesc_bf16_f32(128, 64, 0, 1);   // dV, dK: B MN-major
       constexpr uint32_t idQ = idesc_bf16_f32(128, 64, 1, 1);    // dQ: A and B MN-major
       const uint32_t sK = smem_u32(smem + OFF_K), sV = smem_u32(smem + OFF_V);
-      const uint32_t sP = smem_u32(smem + OFF_P), sDS = smem_u32(smem + OFF_DS);
+      const uint32_t sDS = smem_u32(smem + OFF_DS);
       bool ok = mbar_wait(kv_full, 0, ab);
       for (int it = 0; ok && it < n_it; ++it) {
         const int slot = it & 1;
@@ -437,8 +438,8 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < BQ / 16; ++kk) {
             const uint32_t a_off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_f16_ss(tmem + COL_DV, sdesc_sw128(sP + a_off, 16, 1024), sdesc_sw128(sDO + kk * 2048, 8192, 1024),
-                        idKV, (it > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_ts(tmem + COL_DV, tmem + COL_PT + kk * 8, sdesc_sw128(sDO + kk * 2048, 8192, 1024), idKV,
+                        (it > 0 || kk > 0) ? 1u : 0u);
             umma_f16_ss(tmem + COL_DK, sdesc_sw128(sDS + a_off, 16, 1024), sdesc_sw128(sQ + kk * 2048, 8192, 1024),
                         idKV, (it > 0 || kk > 0) ? 1u : 0u);
           }
@@ -467,7 +468,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     const int t = (warp - 2) * 32 + lane;  // loader index: threads 0..127 stage L / D
     const int kv = jb * BKV + r;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    const uint32_t sP = smem_u32(smem + OFF_P), sDS = smem_u32(smem + OFF_DS);
+    const uint32_t sDS = smem_u32(smem + OFF_DS);
     const float* Lh = p.L + (long long)head * p.s;
     const float* Dh = p.D + (long long)head * p.s;
     float l_next, d_next;
@@ -520,12 +521,12 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
           dd[e / 2] = pack_bf16x2(dv[0], dv[1]);
         }
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          const uint32_t off = sw128_off(r, c * 4 + v);
-          st_shared_v4(sP + off, pp[4 * v], pp[4 * v + 1], pp[4 * v + 2], pp[4 * v + 3]);
-          st_shared_v4(sDS + off, dd[4 * v], dd[4 * v + 1], dd[4 * v + 2], dd[4 * v + 3]);
-        }
+        for (int v = 0; v < 4; ++v)
+          st_shared_v4(sDS + sw128_off(r, c * 4 + v), dd[4 * v], dd[4 * v + 1], dd[4 * v + 2], dd[4 * v + 3]);
+        // P^T (bf16 pairs) into TMEM: 32 query columns = 16 packed columns
+        tmem_st16(trow + COL_PT + c * 16, pp);
       }
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(st_free);
       fence_proxy_async_smem();
