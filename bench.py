@@ -40,7 +40,6 @@ UNIT = "tokens/s"
 BATCH, SEQ = 32, 512
 FLOP_PER_TOKEN = 236.2e6           # 6*(matmul params) + causal attention, per token
 HEAD_GEMM_FLOP = 2 * 16384 * 512 * 50257  # one LM-head forward GEMM at bs32/seq512
-ATTN_FWD_BWD_FLOP = 3.758e9        # configs[0]: BH 32, S 512, d 64 causal (fwd 1.074 + bwd 2.5x)
 
 
 def peaks():
@@ -152,26 +151,33 @@ def run_reference(args, rank):
 
 
 def flash_op_tflops(dev, iters=20):
-    """causal attention fwd+bwd, BH=32, S=512, d=64, bf16; back-to-back
-    launches timed with CUDA events."""
+    """Causal attention fwd+bwd TFLOP/s (bf16, d=64), back-to-back launches timed
+    with CUDA events: configs[0] (BH 32, S 512) and, for context, the full-model
+    shapes (BH 256 x S 512 inside the bs32 step, BH 64 x S 4096 long context).
+    FLOPs: fwd 4*BH*S^2*d/2, bwd 2.5x fwd (no recompute counted)."""
     import torch
     from nlearn_b200 import attention as A
-    torch.manual_seed(0)
-    Q, K, V, dO = (torch.randn(32, 512, 64, device=dev).bfloat16() for _ in range(4))
-    for _ in range(3):
-        O, L = A._flash_fwd_raw(Q, K, V)
-        A._flash_bwd_raw(Q, K, V, O, L, dO)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(iters):
-        O, L = A._flash_fwd_raw(Q, K, V)
-        A._flash_bwd_raw(Q, K, V, O, L, dO)
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / iters
-    return {"config": "BH=32 S=512 d=64 causal bf16 (configs[0])", "ms_fwd_bwd": ms,
-            "tflops": ATTN_FWD_BWD_FLOP / (ms * 1e-3) / 1e12}
+    out = {}
+    for name, n, s in (("configs[0] BH=32 S=512", 32, 512), ("BH=256 S=512", 256, 512), ("BH=64 S=4096", 64, 4096)):
+        torch.manual_seed(0)
+        Q, K, V, dO = (torch.randn(n, s, 64, device=dev).bfloat16() for _ in range(4))
+        for _ in range(3):
+            O, L = A._flash_fwd_raw(Q, K, V)
+            A._flash_bwd_raw(Q, K, V, O, L, dO)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(iters):
+            O, L = A._flash_fwd_raw(Q, K, V)
+            A._flash_bwd_raw(Q, K, V, O, L, dO)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        flop = 3.5 * 4 * n * s * s * 64 / 2
+        out[name] = {"ms_fwd_bwd": ms, "tflops": flop / (ms * 1e-3) / 1e12}
+    c0 = out["configs[0] BH=32 S=512"]
+    return {"config": "BH=32 S=512 d=64 causal bf16 (configs[0])", "ms_fwd_bwd": c0["ms_fwd_bwd"],
+            "tflops": c0["tflops"], "shapes": out}
 
 
 def long_context(dev, rank, world, steps=5, warmup=3):
