@@ -151,33 +151,53 @@ def run_reference(args, rank):
 
 
 def flash_op_tflops(dev, iters=20):
-    """Causal attention fwd+bwd TFLOP/s (bf16, d=64), back-to-back launches timed
-    with CUDA events: configs[0] (BH 32, S 512) and, for context, the full-model
-    shapes (BH 256 x S 512 inside the bs32 step, BH 64 x S 4096 long context).
-    FLOPs: fwd 4*BH*S^2*d/2, bwd 2.5x fwd (no recompute counted)."""
+    """Causal attention fwd+bwd TFLOP/s (bf16, d=64): configs[0] (BH 32, S 512)
+    and, for context, the full-model shapes (BH 256 x S 512 inside the bs32
+    step, BH 64 x S 4096 long context).  Two timings per shape, both CUDA
+    events: `eager` (back-to-back calls through the Python binding, host
+    dispatch included) and `graph` (the same fwd+bwd captured once in a CUDA
+    graph and replayed, i.e. device time of the four kernels).  The headline
+    `tflops` is the graph figure.  FLOPs: fwd 4*BH*S^2*d/2, bwd 2.5x fwd."""
     import torch
     from nlearn_b200 import attention as A
     out = {}
     for name, n, s in (("configs[0] BH=32 S=512", 32, 512), ("BH=256 S=512", 256, 512), ("BH=64 S=4096", 64, 4096)):
         torch.manual_seed(0)
         Q, K, V, dO = (torch.randn(n, s, 64, device=dev).bfloat16() for _ in range(4))
-        for _ in range(3):
+
+        def step():
             O, L = A._flash_fwd_raw(Q, K, V)
             A._flash_bwd_raw(Q, K, V, O, L, dO)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        e0.record()
-        for _ in range(iters):
-            O, L = A._flash_fwd_raw(Q, K, V)
-            A._flash_bwd_raw(Q, K, V, O, L, dO)
-        e1.record()
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / iters
+
+        def timed(fn):
+            for _ in range(3):
+                fn()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(iters):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / iters
+
         flop = 3.5 * 4 * n * s * s * 64 / 2
-        out[name] = {"ms_fwd_bwd": ms, "tflops": flop / (ms * 1e-3) / 1e12}
+        ms_eager = timed(step)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            step()  # warm-up on the capture stream
+        torch.cuda.current_stream(dev).wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        ms_graph = timed(g.replay)
+        del g
+        out[name] = {"ms_fwd_bwd": ms_graph, "tflops": flop / (ms_graph * 1e-3) / 1e12,
+                     "eager_ms_fwd_bwd": ms_eager, "eager_tflops": flop / (ms_eager * 1e-3) / 1e12}
     c0 = out["configs[0] BH=32 S=512"]
-    return {"config": "BH=32 S=512 d=64 causal bf16 (configs[0])", "ms_fwd_bwd": c0["ms_fwd_bwd"],
-            "tflops": c0["tflops"], "shapes": out}
+    return {"config": "BH=32 S=512 d=64 causal bf16 (configs[0])", "timing": "CUDA-graph replay of fwd+bwd",
+            "ms_fwd_bwd": c0["ms_fwd_bwd"], "tflops": c0["tflops"], "shapes": out}
 
 
 def long_context(dev, rank, world, steps=5, warmup=3):
