@@ -319,9 +319,18 @@ __device__ __forceinline__ void slot_reuse_wait(int lane) {
   if (lane == 0) bulk_wait_read_all();
   __syncwarp();
 }
+// A 32x32 bf16 block fills half of the 4 KB slot, so consecutive blocks
+// alternate halves and only the store issued two blocks ago must have read
+// its half: the staging of block i overlaps the store of block i-1.
+__device__ __forceinline__ uint8_t* half_slot(uint8_t* slot, int lane, uint32_t& nblk) {
+  if (lane == 0) bulk_wait_read<1>();
+  __syncwarp();
+  return slot + ((nblk++ & 1u) << 11);
+}
 
 __device__ __forceinline__ void epi_chunk_tma(const Params& p, const CUtensorMap* tmC, const CUtensorMap* tmX,
-                                              uint8_t* slot, int lane, int row, int row0, int col0, float (&v)[32]) {
+                                              uint8_t* slot, uint32_t& nblk, int lane, int row, int row0, int col0,
+                                              float (&v)[32]) {
   const bool in = row < p.M;
   const int epi = p.epi;
 #pragma unroll
@@ -332,8 +341,8 @@ __device__ __forceinline__ void epi_chunk_tma(const Params& p, const CUtensorMap
   }
   const long long off = (long long)row * p.ldc + col0;
   const bool full = col0 + 32 <= p.N;
-  slot_reuse_wait(lane);
-  if (epi == NL_EPI_BIAS_GELU) {  // aux = pre-activation, C = gelu(pre): two bf16 halves of the slot
+  if (epi == NL_EPI_BIAS_GELU) {
+    slot_reuse_wait(lane);  // aux = pre-activation, C = gelu(pre): two bf16 halves of the slot
     stage_bf16(slot, lane, v);
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
@@ -388,8 +397,13 @@ __device__ __forceinline__ void epi_chunk_tma(const Params& p, const CUtensorMap
       for (int i = 0; i < 32; ++i) v[i] += (col0 + i < p.N) ? rf[i] : 0.f;
     }
   }
-  if (p.c_bf16) stage_bf16(slot, lane, v);
-  else stage_f32(slot, lane, v);
+  if (p.c_bf16) {
+    slot = half_slot(slot, lane, nblk);
+    stage_bf16(slot, lane, v);
+  } else {
+    slot_reuse_wait(lane);
+    stage_f32(slot, lane, v);
+  }
   flush_block(tmC, slot, lane, col0, row0, epi == NL_EPI_ACCUM);
 }
 
@@ -415,6 +429,7 @@ __device__ __forceinline__ void epilogue_role(const Params& p, uint32_t tmem_bas
   const int half = (warp - 2) >> 2;
   int acc = 0;
   uint32_t acc_ph = 0;
+  uint32_t nblk = 0;
   for (int u = cta_unit0; half < split && u < num_units; u += cta_stride) {
     int mb, nb, sk;
     decode_unit(p, u, mb, nb, sk);
@@ -442,9 +457,23 @@ __device__ __forceinline__ void epilogue_role(const Params& p, uint32_t tmem_bas
       float v[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-      if (!lce) epi_chunk(p, row, col0, v);
-      else if (p.epi == NL_EPI_LCE_STATS) lce_stats_chunk(p, row, col0, v, m, ssum, tl, t);
-      else lce_grad_chunk(p, row, col0, v, lse2, t, gsc);
+      if (p.epi == NL_EPI_LCE_STATS) {
+        lce_stats_chunk(p, row, col0, v, m, ssum, tl, t);
+      } else if (p.tma_out) {  // warp-uniform: rows >= M stage garbage that the TMA store clips
+        const int row0 = mb * unit_rows + row_off + q * 32;
+        if (p.epi == NL_EPI_LCE_GRAD) {
+          lce_grad_values(p, col0, v, lse2, t, gsc);
+          uint8_t* h = half_slot(slot, lane, nblk);
+          stage_bf16(h, lane, v);
+          flush_block(tmC, h, lane, col0, row0, false);
+        } else {
+          epi_chunk_tma(p, tmC, tmX, slot, nblk, lane, row, row0, col0, v);
+        }
+      } else if (!lce) {
+        epi_chunk(p, row, col0, v);
+      } else {
+        lce_grad_chunk(p, row, col0, v, lse2, t, gsc);
+      }
     }
     if (p.epi == NL_EPI_LCE_STATS && row < p.M) {
       m *= 0.6931471805599453f;  // base-2 max -> natural units
