@@ -447,16 +447,32 @@ __device__ __forceinline__ void epilogue_role(const Params& p, uint32_t tmem_bas
         gsc = p.grad_scale * (p.gptr ? *p.gptr : 1.f);
       }
     }
+    // The load of chunk c+1 is in flight while chunk c is processed; the
+    // accumulator goes back to the MMA warp as soon as its last chunk is in
+    // registers.
+    auto release = [&]() {
+      tc_fence_before();
+      if (remote) mbar_arrive_cluster(acc ? tempty1 : tempty0);
+      else mbar_arrive(reinterpret_cast<uint64_t*>(__cvta_shared_to_generic(acc ? tempty1 : tempty0)));
+    };
+    bool released = false;
+    const int c_begin = half * (BN / 32 / split), c_end = (half + 1) * (BN / 32 / split);
+    uint32_t r[32];
+    if (nb * BN + c_begin * 32 < p.N) tmem_ld32(taddr + c_begin * 32, r);
 #pragma unroll 1
-    for (int c = half * (BN / 32 / split); c < (half + 1) * (BN / 32 / split); ++c) {
+    for (int c = c_begin; c < c_end; ++c) {
       const int col0 = nb * BN + c * 32;
       if (col0 >= p.N) break;  // warp-uniform
-      uint32_t r[32];
-      tmem_ld32(taddr + c * 32, r);
-      tmem_wait_ld();
+      tmem_wait_ld_tied(r);
       float v[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      if (c + 1 < c_end && col0 + 32 < p.N) {
+        tmem_ld32(taddr + (c + 1) * 32, r);
+      } else {
+        release();
+        released = true;
+      }
       if (p.epi == NL_EPI_LCE_STATS) {
         lce_stats_chunk(p, row, col0, v, m, ssum, tl, t);
       } else if (p.tma_out) {  // warp-uniform: rows >= M stage garbage that the TMA store clips
@@ -482,9 +498,7 @@ __device__ __forceinline__ void epilogue_role(const Params& p, uint32_t tmem_bas
       const int c0 = nb * BN + half * (BN / split);
       if (t >= c0 && t < c0 + BN / split && t < p.N) p.tgt_logit[row] = tl;
     }
-    tc_fence_before();
-    if (remote) mbar_arrive_cluster(acc ? tempty1 : tempty0);
-    else mbar_arrive(reinterpret_cast<uint64_t*>(__cvta_shared_to_generic(acc ? tempty1 : tempty0)));
+    if (!released) release();
     acc ^= 1;
     if (acc == 0) acc_ph ^= 1;
   }
