@@ -906,7 +906,9 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
   int BN = 256;
   {
     const long long t256 = (long long)((M + BM - 1) / BM) * ((N + 255) / 256);
-    if (N <= 128 || t256 < sms) BN = 128;
+    // accumulating GEMMs with a long K fill the machine by splitting K instead
+    const bool split_fills = epi == NL_EPI_ACCUM && p.num_kb >= 64;
+    if (N <= 128 || (t256 < sms && !split_fills)) BN = 128;
     if (ex && ex->force_bn) BN = ex->force_bn;
     static int fbn = -1;
     if (fbn < 0) {
@@ -941,7 +943,7 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
   p.split_k = 1;
   if (epi == NL_EPI_ACCUM && p.num_kb >= 16) {
     double best = 0.0;
-    const int smax = p.num_kb / 8 < 16 ? p.num_kb / 8 : 16;
+    const int smax = p.num_kb / 8 < 32 ? p.num_kb / 8 : 32;
     for (int sk = 1; sk <= smax; ++sk) {
       const long long units = (long long)tiles * sk;
       const long long waves = (units + wk - 1) / wk;

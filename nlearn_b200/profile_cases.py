@@ -41,6 +41,7 @@ def main(argv=None):
     ap.add_argument("--chunk", type=int, default=0)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--pad", type=int, default=0, help="extra elements of row pitch for the GEMM operands")
+    ap.add_argument("--accum", action="store_true", help="GEMM into an f32 accumulator (weight-gradient form)")
     a = ap.parse_args(argv)
     dev = torch.device("cuda:0")
     torch.manual_seed(0)
@@ -73,9 +74,14 @@ def main(argv=None):
             return torch.randn(r, c + a.pad, device=dev).bfloat16()[:, :c]
         A = mk(*((K, M) if at else (M, K)))
         B = mk(*((N, K) if bt else (K, N)))
-        C = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
-        ms = _time(lambda: gemm_ex(A, B, a_trans=at, b_trans=bt, out=C), a.iters)
-        out.update(M=M, N=N, K=K, layout=a.layout, pad=a.pad, ms=ms, tflops=2 * M * N * K / ms / 1e9)
+        if a.accum:
+            from .kernels.gemm import EPI_ACCUM
+            C = torch.zeros(M, N, device=dev, dtype=torch.float32)
+            ms = _time(lambda: gemm_ex(A, B, a_trans=at, b_trans=bt, out=C, epilogue=EPI_ACCUM), a.iters)
+        else:
+            C = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            ms = _time(lambda: gemm_ex(A, B, a_trans=at, b_trans=bt, out=C), a.iters)
+        out.update(M=M, N=N, K=K, layout=a.layout, pad=a.pad, accum=a.accum, ms=ms, tflops=2 * M * N * K / ms / 1e9)
     elif a.case in ("attn_fwd", "attn_bwd"):
         from . import attention as A
         n, s = a.heads, a.seq
