@@ -102,6 +102,11 @@ __device__ __forceinline__ void decode_unit(const Params& p, int u, int& mb, int
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Epilogue families, one kernel instantiation each.
+constexpr int kEpiGeneric = 0;   // STORE / ACCUM / BIAS / BIAS_GELU / RESID / DGELU
+constexpr int kEpiLceStats = 1;  // LCE_STATS
+constexpr int kEpiLceGrad = 2;   // LCE_GRAD
+
 // Online (max, sum-exp) of 32 logits of one row, the max kept in base-2 units
 // (y = x log2 e, so each term is one MUFU ex2); padding columns masked.  (A
 // natural-units variant with a separate max pass measured 20-40 % slower.)
@@ -411,8 +416,10 @@ __device__ __forceinline__ void epi_chunk_tma(const Params& p, const CUtensorMap
 // fused epilogue, and release the TMEM buffer by arriving on tempty (a local
 // barrier, or the pair leader's via its cluster address).  `unit_rows` is the
 // M extent of one work unit (128, or 256 for a CTA pair) and `row_off` this
-// CTA's first row inside it.
-template <int BN>
+// CTA's first row inside it.  EK selects the epilogue family at compile time
+// (kEpiGeneric / kEpiLceStats / kEpiLceGrad) so that each kernel carries only
+// the code of its own family.
+template <int BN, int EK>
 __device__ __forceinline__ void epilogue_role(const Params& p, uint32_t tmem_base, uint64_t* tfull_bar,
                                               uint32_t tempty0, uint32_t tempty1, bool remote, int unit_rows,
                                               int row_off, const Abort& ab, const CUtensorMap* tmC,
@@ -437,12 +444,11 @@ __device__ __forceinline__ void epilogue_role(const Params& p, uint32_t tmem_bas
     tc_fence_after();
     const int row = mb * unit_rows + row_off + q * 32 + lane;
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-    const bool lce = p.epi >= NL_EPI_LCE_STATS;
     int t = -1;
     float lse2 = 0.f, gsc = 0.f, m = -INFINITY, ssum = 0.f, tl = 0.f;
-    if (lce && row < p.M) {
+    if (EK != kEpiGeneric && row < p.M) {
       t = p.targets[row] - p.col_offset;
-      if (p.epi == NL_EPI_LCE_GRAD) {
+      if (EK == kEpiLceGrad) {
         lse2 = p.lse[row] * kLog2e;
         gsc = p.grad_scale * (p.gptr ? *p.gptr : 1.f);
       }
@@ -473,25 +479,25 @@ __device__ __forceinline__ void epilogue_role(const Params& p, uint32_t tmem_bas
         release();
         released = true;
       }
-      if (p.epi == NL_EPI_LCE_STATS) {
+      // TMA-store paths are warp-uniform: rows >= M stage garbage that the store clips
+      const int row0 = mb * unit_rows + row_off + q * 32;
+      if constexpr (EK == kEpiLceStats) {
         lce_stats_chunk(p, row, col0, v, m, ssum, tl, t);
-      } else if (p.tma_out) {  // warp-uniform: rows >= M stage garbage that the TMA store clips
-        const int row0 = mb * unit_rows + row_off + q * 32;
-        if (p.epi == NL_EPI_LCE_GRAD) {
+      } else if constexpr (EK == kEpiLceGrad) {
+        if (p.tma_out) {
           lce_grad_values(p, col0, v, lse2, t, gsc);
           uint8_t* h = half_slot(slot, lane, nblk);
           stage_bf16(h, lane, v);
           flush_block(tmC, h, lane, col0, row0, false);
         } else {
-          epi_chunk_tma(p, tmC, tmX, slot, nblk, lane, row, row0, col0, v);
+          lce_grad_chunk(p, row, col0, v, lse2, t, gsc);
         }
-      } else if (!lce) {
-        epi_chunk(p, row, col0, v);
       } else {
-        lce_grad_chunk(p, row, col0, v, lse2, t, gsc);
+        if (p.tma_out) epi_chunk_tma(p, tmC, tmX, slot, nblk, lane, row, row0, col0, v);
+        else epi_chunk(p, row, col0, v);
       }
     }
-    if (p.epi == NL_EPI_LCE_STATS && row < p.M) {
+    if (EK == kEpiLceStats && row < p.M) {
       m *= 0.6931471805599453f;  // base-2 max -> natural units
       p.part[(long long)(2 * nb + half) * p.M + row] = make_float2(m, ssum);
       if (split == 1) p.part[(long long)(2 * nb + 1) * p.M + row] = make_float2(-INFINITY, 0.f);
@@ -505,7 +511,7 @@ __device__ __forceinline__ void epilogue_role(const Params& p, uint32_t tmem_bas
   if (lane == 0) bulk_wait_all();  // stores complete before the CTA retires
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, int EK>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX, Params p) {
@@ -619,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    epilogue_role<BN>(p, tmem_base, tfull_bar, smem_u32(tempty_bar), smem_u32(tempty_bar + 1), false, BM, 0, ab,
+    epilogue_role<BN, EK>(p, tmem_base, tfull_bar, smem_u32(tempty_bar), smem_u32(tempty_bar + 1), false, BM, 0, ab,
                       &tmC, &tmX, tiles + C::STAGES * C::STAGE_BYTES);
   }
 
@@ -630,11 +636,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, int EK>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& tx, Params& p,
            cudaStream_t stream) {
   using C = Cfg<BN>;
-  auto kern = gemm_kernel<BN, A_MN, B_MN>;
+  auto kern = gemm_kernel<BN, A_MN, B_MN, EK>;
   static int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -649,6 +655,21 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
   return launch_status();
 }
 
+
+template <int EK>
+int launch_layout(int BN, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                  const CUtensorMap& tx, Params& p, cudaStream_t stream) {
+  if (BN == 256) {
+    if (!a_mn && !b_mn) return launch<256, false, false, EK>(ta, tb, tc, tx, p, stream);
+    if (!a_mn && b_mn) return launch<256, false, true, EK>(ta, tb, tc, tx, p, stream);
+    if (a_mn && !b_mn) return launch<256, true, false, EK>(ta, tb, tc, tx, p, stream);
+    return launch<256, true, true, EK>(ta, tb, tc, tx, p, stream);
+  }
+  if (!a_mn && !b_mn) return launch<128, false, false, EK>(ta, tb, tc, tx, p, stream);
+  if (!a_mn && b_mn) return launch<128, false, true, EK>(ta, tb, tc, tx, p, stream);
+  if (a_mn && !b_mn) return launch<128, true, false, EK>(ta, tb, tc, tx, p, stream);
+  return launch<128, true, true, EK>(ta, tb, tc, tx, p, stream);
+}
 
 // ============================================================== CTA-pair GEMM
 // Same roles as gemm_kernel, but a 2-CTA cluster computes 256 x 256 tiles with
@@ -791,7 +812,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    epilogue_role<BN2>(p, tmem_base, tfull_bar, mapa_shared(smem_u32(&tempty_bar[0]), 0),
+    epilogue_role<BN2, kEpiGeneric>(p, tmem_base, tfull_bar, mapa_shared(smem_u32(&tempty_bar[0]), 0),
                        mapa_shared(smem_u32(&tempty_bar[1]), 0), true, BM2, static_cast<int>(rank) * 128, ab, &tmC,
                        &tmX, tiles + STAGES * STAGE_BYTES);
   }
@@ -926,6 +947,7 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
   }
   // (measured: pairs win from K >= 1024; at K = 512 the single-CTA kernel is faster)
   bool use_pair = pair_enabled == 1 ? (BN == 256 && p.num_kb >= 16) : (pair_enabled == 2 && BN == 256);
+  if (epi >= NL_EPI_LCE_STATS) use_pair = false;  // the LCE epilogues run on single-CTA tiles
   const int workers = use_pair ? sms / 2 : sms;
   const int unit_m = use_pair ? pair::BM2 : BM;
   if (use_pair) {
@@ -982,16 +1004,10 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
     if (a_mn && !b_mn) return launch_pair<true, false>(ta, tb, tc, tx, p, stream);
     return launch_pair<true, true>(ta, tb, tc, tx, p, stream);
   }
-  if (BN == 256) {
-    if (!a_mn && !b_mn) return launch<256, false, false>(ta, tb, tc, tx, p, stream);
-    if (!a_mn && b_mn) return launch<256, false, true>(ta, tb, tc, tx, p, stream);
-    if (a_mn && !b_mn) return launch<256, true, false>(ta, tb, tc, tx, p, stream);
-    return launch<256, true, true>(ta, tb, tc, tx, p, stream);
-  }
-  if (!a_mn && !b_mn) return launch<128, false, false>(ta, tb, tc, tx, p, stream);
-  if (!a_mn && b_mn) return launch<128, false, true>(ta, tb, tc, tx, p, stream);
-  if (a_mn && !b_mn) return launch<128, true, false>(ta, tb, tc, tx, p, stream);
-  return launch<128, true, true>(ta, tb, tc, tx, p, stream);
+  const int ek = epi == NL_EPI_LCE_STATS ? kEpiLceStats : epi == NL_EPI_LCE_GRAD ? kEpiLceGrad : kEpiGeneric;
+  if (ek == kEpiLceStats) return launch_layout<kEpiLceStats>(BN, a_mn, b_mn, ta, tb, tc, tx, p, stream);
+  if (ek == kEpiLceGrad) return launch_layout<kEpiLceGrad>(BN, a_mn, b_mn, ta, tb, tc, tx, p, stream);
+  return launch_layout<kEpiGeneric>(BN, a_mn, b_mn, ta, tb, tc, tx, p, stream);
 }
 
 }  // namespace nl
