@@ -125,8 +125,10 @@ __device__ __forceinline__ void lce_stats_chunk(const Params& p, int row, int co
     s *= ex2_approx(m - mx);
     m = mx;
   }
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};  // four partial sums: shorter FADD chains
 #pragma unroll
-  for (int i = 0; i < 32; ++i) s += ex2_approx(y[i] - m);
+  for (int i = 0; i < 32; ++i) s4[i & 3] += ex2_approx(y[i] - m);
+  s += (s4[0] + s4[1]) + (s4[2] + s4[3]);
 }
 
 // dlogits = (softmax - onehot) * scale for 32 columns, bf16 out; padding -> 0.
