@@ -181,11 +181,22 @@ __device__ __forceinline__ void lce_grad_chunk(const Params& p, int row, int col
 // dlogits values (f32) of 32 columns for the staged-store path; padding -> 0.
 __device__ __forceinline__ void lce_grad_values(const Params& p, int col0, float (&v)[32], float lse2, int t,
                                                 float scale) {
+  // (2^(x log2 e - lse log2 e) - [c == t]) * scale: one FFMA, one ex2, one FMUL
+  // per column; the one-hot term only in the chunk that holds the target.
+  const float nl = -lse2;
+  const int valid = p.v_valid - col0;
+  if (valid >= 32) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const int c = col0 + i;
-    const float pr = ex2_approx(v[i] * kLog2e - lse2);
-    v[i] = (c < p.v_valid) ? (pr - (c == t ? 1.f : 0.f)) * scale : 0.f;
+    for (int i = 0; i < 32; ++i) v[i] = ex2_approx(fmaf(v[i], kLog2e, nl)) * scale;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = (i < valid) ? ex2_approx(fmaf(v[i], kLog2e, nl)) * scale : 0.f;
+  }
+  const int ti = t - col0;
+  if (static_cast<unsigned>(ti) < 32u && ti < valid) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i == ti) v[i] -= scale;
   }
 }
 
