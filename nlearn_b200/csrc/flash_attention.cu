@@ -316,7 +316,8 @@ constexpr int OFF_Q = 2 * TILE;   // 2 slots
 constexpr int OFF_DO = 4 * TILE;  // 2 slots
 constexpr int OFF_DS = 6 * TILE;  // 32 KB  dS^T [kv rows, q cols]
 constexpr int OFF_LD = 8 * TILE;  // L2[2][128], D[2][128] f32
-constexpr int OFF_BAR = OFF_LD + 2048;
+constexpr int OFF_DQS = OFF_LD + 2048;  // dQ staging: 4 warps x two 32x32 f32 boxes (SW128)
+constexpr int OFF_BAR = OFF_DQS + 4 * 8192;
 constexpr int SMEM = OFF_BAR + 256;
 constexpr int TMEM_COLS = 512;
 constexpr int COL_S = 0, COL_DP = 128, COL_DV = 256, COL_DK = 320, COL_DQ = 384;
@@ -339,7 +340,7 @@ struct BwdParams {
 __global__ void __launch_bounds__(bwd::kThreads, 1)
     flash_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                     BwdParams p) {
+                     const __grid_constant__ CUtensorMap tmDQ, BwdParams p) {
   using namespace bwd;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -498,27 +499,39 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       tc_fence_after();
       const float* Lb = Lbuf + buf * 128;
       const float* Db = Dbuf + buf * 128;
+      // the causal / sequence-end mask is needed only on the diagonal tile and
+      // on a ragged last query tile (warp-uniform)
+      const bool masked = (i == jb) || ((i + 1) * BQ > p.s);
 #pragma unroll 1
       for (int c = 2 * half; c < 2 * half + 2; ++c) {
         uint32_t us[32], ud[32];
         tmem_ld32(trow + COL_S + c * 32, us);
         tmem_ld32(trow + COL_DP + c * 32, ud);
+        float nl[32], dcol[32];  // -L (base 2) and D of the 32 query columns: broadcast vector loads
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          const float4 l4 = reinterpret_cast<const float4*>(Lb + c * 32)[v];
+          const float4 d4 = reinterpret_cast<const float4*>(Db + c * 32)[v];
+          nl[4 * v] = -l4.x; nl[4 * v + 1] = -l4.y; nl[4 * v + 2] = -l4.z; nl[4 * v + 3] = -l4.w;
+          dcol[4 * v] = d4.x; dcol[4 * v + 1] = d4.y; dcol[4 * v + 2] = d4.z; dcol[4 * v + 3] = d4.w;
+        }
         tmem_wait_ld();
+        float pv[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) pv[e] = ex2_approx(fmaf(__uint_as_float(us[e]), p.sl2, nl[e]));
+        if (masked) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int qg = i * BQ + c * 32 + e;
+            pv[e] = (qg >= kv && qg < p.s) ? pv[e] : 0.f;  // causal (query >= key), in range
+          }
+        }
         uint32_t pp[16], dd[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          float pv[2], dv[2];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int qc = c * 32 + e + h;
-            const int qg = i * BQ + qc;
-            float pr = ex2_approx(__uint_as_float(us[e + h]) * p.sl2 - Lb[qc]);
-            pr = (qg >= kv && qg < p.s) ? pr : 0.f;  // causal (query >= key), in range
-            pv[h] = pr;
-            dv[h] = pr * (__uint_as_float(ud[e + h]) - Db[qc]);
-          }
-          pp[e / 2] = pack_bf16x2(pv[0], pv[1]);
-          dd[e / 2] = pack_bf16x2(dv[0], dv[1]);
+          pp[e / 2] = pack_bf16x2(pv[e], pv[e + 1]);
+          dd[e / 2] = pack_bf16x2(pv[e] * (__uint_as_float(ud[e]) - dcol[e]),
+                                  pv[e + 1] * (__uint_as_float(ud[e + 1]) - dcol[e + 1]));
         }
 #pragma unroll
         for (int v = 0; v < 4; ++v)
@@ -558,12 +571,15 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------- dQ warps (one query row each)
+    // Each warp stages its 32 rows x 64 columns of the dQ tile as two 32 x 32
+    // f32 boxes in the swizzled layout of the dQacc tensor map and adds them
+    // to dQacc with TMA reduce-adds (rows past s are clipped per head).
     if (p.want_dq) {
       const int quarter = warp & 3;
-      const int r = quarter * 32 + lane;
       const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+      uint8_t* stg = smem + OFF_DQS + (warp - 10) * 8192;
       for (int it = 0; it < n_it; ++it) {
-        const int q = (jb + it) * BQ + r;
+        const int q0 = (jb + it) * BQ + quarter * 32;
         if (!mbar_wait_warp(dq_full, it & 1, ab)) break;
         tc_fence_after();
         uint32_t u0[32], u1[32];
@@ -572,18 +588,23 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(dq_free);
-        if (q < p.s) {
-          float4* dst = reinterpret_cast<float4*>(p.dQacc + ((long long)head * p.s + q) * HD);
+        if (lane == 0) bulk_wait_read_all();  // the previous reduce has read the staging
+        __syncwarp();
+        const uint32_t b0 = smem_u32(stg) + lane * 128;
 #pragma unroll
-          for (int v = 0; v < 8; ++v)
-            atomicAdd(dst + v, make_float4(__uint_as_float(u0[4 * v]), __uint_as_float(u0[4 * v + 1]),
-                                           __uint_as_float(u0[4 * v + 2]), __uint_as_float(u0[4 * v + 3])));
-#pragma unroll
-          for (int v = 0; v < 8; ++v)
-            atomicAdd(dst + 8 + v, make_float4(__uint_as_float(u1[4 * v]), __uint_as_float(u1[4 * v + 1]),
-                                               __uint_as_float(u1[4 * v + 2]), __uint_as_float(u1[4 * v + 3])));
+        for (int j = 0; j < 8; ++j) {
+          st_shared_v4(b0 + ((j ^ (lane & 7)) << 4), u0[4 * j], u0[4 * j + 1], u0[4 * j + 2], u0[4 * j + 3]);
+          st_shared_v4(b0 + 4096 + ((j ^ (lane & 7)) << 4), u1[4 * j], u1[4 * j + 1], u1[4 * j + 2], u1[4 * j + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && q0 < p.s) {
+          tma_reduce_add_3d(&tmDQ, stg, 0, q0, head);
+          tma_reduce_add_3d(&tmDQ, stg + 4096, 32, q0, head);
+          bulk_commit();
         }
       }
+      if (lane == 0) bulk_wait_all();
     }
   }
 
@@ -730,11 +751,13 @@ int flash_bwd(const void* Q, const void* K, const void* V, fa::Strides qs, const
         want_dq ? dQacc : nullptr, rows);
     if ((st = launch_status())) return st;
   }
-  CUtensorMap tq, tk, tv, tdo;
+  CUtensorMap tq, tk, tv, tdo, tdq;
   if ((st = make_tmap_bf16_4d(&tq, Q, s, H, B, qs.s, qs.h, qs.b, BQ))) return st;
   if ((st = make_tmap_bf16_4d(&tk, K, s, H, B, qs.s, qs.h, qs.b, BKV))) return st;
   if ((st = make_tmap_bf16_4d(&tv, V, s, H, B, qs.s, qs.h, qs.b, BKV))) return st;
   if ((st = make_tmap_bf16_4d(&tdo, dO, s, H, B, os.s, os.h, os.b, BQ))) return st;
+  memset(&tdq, 0, sizeof(tdq));
+  if (want_dq && (st = make_tmap_f32_rows64_3d(&tdq, dQacc, s, n))) return st;
   BwdParams p{};
   p.L = L;
   p.D = D;
@@ -753,7 +776,7 @@ int flash_bwd(const void* Q, const void* K, const void* V, fa::Strides qs, const
   p.err = device_error_word();
   if ((st = set_smem(flash_bwd_kernel, bwd::SMEM))) return st;
   const long long grid = static_cast<long long>(n) * p.nq;
-  flash_bwd_kernel<<<static_cast<unsigned>(grid), bwd::kThreads, bwd::SMEM, stream>>>(tq, tk, tv, tdo, p);
+  flash_bwd_kernel<<<static_cast<unsigned>(grid), bwd::kThreads, bwd::SMEM, stream>>>(tq, tk, tv, tdo, tdq, p);
   if ((st = launch_status())) return st;
   if (want_dq) {
     const long long n8 = rows * HD / 8;

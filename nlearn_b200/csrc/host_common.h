@@ -98,6 +98,22 @@ inline int make_tmap_bf16_4d(CUtensorMap* m, const void* base, uint64_t rows, ui
   return r == CUDA_SUCCESS ? NL_OK : NL_ERR_CUDA;
 }
 
+// f32 [n, rows, 64] (contiguous) written by 32 x 32 boxes with 128-byte
+// swizzle (one row of a box = 128 B); rows past `rows` are clipped per n.
+inline int make_tmap_f32_rows64_3d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t n) {
+  auto fn = encode_tiled_fn();
+  if (!fn) return NL_ERR_CUDA;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return NL_ERR_ALIGN;
+  cuuint64_t dims[3] = {64, rows, n};
+  cuuint64_t strides[2] = {64 * 4, rows * 64 * 4};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NL_OK : NL_ERR_CUDA;
+}
+
 inline int sm_count() {
   int dev = 0, n = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
