@@ -310,12 +310,12 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
 // ====================================================================== backward
 namespace bwd {
 constexpr int kThreads = 14 * 32;  // TMA, MMA, 8 P/dS warps, 4 dQ warps
-constexpr int OFF_K = 0;
-constexpr int OFF_V = TILE;
-constexpr int OFF_Q = 2 * TILE;   // 2 slots
-constexpr int OFF_DO = 4 * TILE;  // 2 slots
-constexpr int OFF_DS = 6 * TILE;  // 32 KB  dS^T [kv rows, q cols]
-constexpr int OFF_LD = 8 * TILE;  // L2[2][128], D[2][128] f32
+constexpr int OFF_K = 0;          // 2 slots (one per work item in flight)
+constexpr int OFF_V = 2 * TILE;   // 2 slots
+constexpr int OFF_Q = 4 * TILE;   // 2 slots
+constexpr int OFF_DO = 6 * TILE;  // 2 slots
+constexpr int OFF_DS = 8 * TILE;  // 32 KB  dS^T [kv rows, q cols]
+constexpr int OFF_LD = 10 * TILE;  // L2[2][128], D[2][128] f32
 constexpr int OFF_DQS = OFF_LD + 2048;  // dQ staging: 4 warps x two 32x32 f32 boxes (SW128)
 constexpr int OFF_BAR = OFF_DQS + 4 * 8192;
 constexpr int SMEM = OFF_BAR + 256;
@@ -337,6 +337,23 @@ struct BwdParams {
   int* err;
 };
 
+// Work item w (0 .. n*nq-1) = (key tile jb = w / n, head = w % n): items are
+// numbered heaviest first (key tile 0 meets every query tile).  Round k deals
+// items k*G .. k*G+G-1 to the G persistent CTAs, forwards in even rounds and
+// backwards in odd ones, which evens out the per-CTA work.
+__device__ __forceinline__ int bwd_round_item(int k) {
+  const int G = static_cast<int>(gridDim.x), b = static_cast<int>(blockIdx.x);
+  return k * G + ((k & 1) ? G - 1 - b : b);
+}
+__device__ __forceinline__ void bwd_item(const BwdParams& p, int w, int& jb, int& head) {
+  jb = w / p.n;
+  head = w - jb * p.n;
+}
+
+// Persistent: one CTA per SM walks its work items; barrier phases run on the
+// CTA's item count (K/V slots, dK/dV accumulator) and its running query-tile
+// iteration count g (everything per iteration), so the S/dP MMAs of an item
+// overlap the dK/dV write-out of the previous one.
 __global__ void __launch_bounds__(bwd::kThreads, 1)
     flash_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -344,34 +361,34 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   using namespace bwd;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* kv_full = bars + 0;
-  uint64_t* qdo_full = bars + 1;   // [2]
-  uint64_t* qdo_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* st_free = bars + 6;
-  uint64_t* ds_full = bars + 7;
-  uint64_t* ds_empty = bars + 8;
-  uint64_t* dq_full = bars + 9;
-  uint64_t* dq_free = bars + 10;
-  uint64_t* acc_done = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* kv_full = bars + 0;    // [2]
+  uint64_t* kv_empty = bars + 2;   // [2]
+  uint64_t* qdo_full = bars + 4;   // [2]
+  uint64_t* qdo_empty = bars + 6;  // [2]
+  uint64_t* s_full = bars + 8;
+  uint64_t* st_free = bars + 9;
+  uint64_t* ds_full = bars + 10;
+  uint64_t* ds_empty = bars + 11;
+  uint64_t* dq_full = bars + 12;
+  uint64_t* dq_free = bars + 13;
+  uint64_t* acc_done = bars + 14;
+  uint64_t* acc_free = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* Lbuf = reinterpret_cast<float*>(smem + OFF_LD);  // [2][128]
   float* Dbuf = Lbuf + 256;                               // [2][128]
 
   const int warp = warp_id(), lane = lane_id();
-  const int jb = static_cast<int>(blockIdx.x) / p.n;  // key tile; jb = 0 has the most work
-  const int head = static_cast<int>(blockIdx.x) % p.n;
-  const int bi = head / p.H, hi = head % p.H;
-  const int n_it = p.nq - jb;
+  const int n_items = p.n * p.nq;
 
   if (smem_u32(smem) & 1023) {
     if (threadIdx.x == 0 && p.err) atomicExch(p.err, 2);
     return;
   }
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
       mbar_init(&qdo_full[i], 1);
       mbar_init(&qdo_empty[i], 1);
     }
@@ -382,6 +399,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 128);
     mbar_init(acc_done, 1);
+    mbar_init(acc_free, 256);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -393,71 +411,94 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   Abort ab{abort_flag, p.err};
 
   if (warp == 0) {
+    // ------------------------------------------------------------ TMA loads
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       tma_prefetch_desc(&tmDO);
-      mbar_expect_tx(kv_full, 2 * TILE);
-      tma_load_4d(&tmK, kv_full, smem + OFF_K, 0, jb * BKV, hi, bi);
-      tma_load_4d(&tmV, kv_full, smem + OFF_V, 0, jb * BKV, hi, bi);
-      for (int it = 0; it < n_it; ++it) {
-        const int slot = it & 1, i = jb + it;
-        if (!mbar_wait(&qdo_empty[slot], ((it >> 1) & 1) ^ 1, ab)) break;
-        mbar_expect_tx(&qdo_full[slot], 2 * TILE);
-        tma_load_4d(&tmQ, &qdo_full[slot], smem + OFF_Q + slot * TILE, 0, i * BQ, hi, bi);
-        tma_load_4d(&tmDO, &qdo_full[slot], smem + OFF_DO + slot * TILE, 0, i * BQ, hi, bi);
+      bool ok = true;
+      int g = 0, wi = 0;
+      for (int w = bwd_round_item(0); ok && w < n_items; w = bwd_round_item(++wi)) {
+        int jb, head;
+        bwd_item(p, w, jb, head);
+        const int bi = head / p.H, hi = head % p.H;
+        const int ks = wi & 1;
+        if (wi >= 2 && !mbar_wait(&kv_empty[ks], ((wi >> 1) - 1) & 1, ab)) break;
+        mbar_expect_tx(&kv_full[ks], 2 * TILE);
+        tma_load_4d(&tmK, &kv_full[ks], smem + OFF_K + ks * TILE, 0, jb * BKV, hi, bi);
+        tma_load_4d(&tmV, &kv_full[ks], smem + OFF_V + ks * TILE, 0, jb * BKV, hi, bi);
+        for (int i = jb; i < p.nq; ++i, ++g) {
+          const int slot = g & 1;
+          if (!mbar_wait(&qdo_empty[slot], ((g >> 1) & 1) ^ 1, ab)) { ok = false; break; }
+          mbar_expect_tx(&qdo_full[slot], 2 * TILE);
+          tma_load_4d(&tmQ, &qdo_full[slot], smem + OFF_Q + slot * TILE, 0, i * BQ, hi, bi);
+          tma_load_4d(&tmDO, &qdo_full[slot], smem + OFF_DO + slot * TILE, 0, i * BQ, hi, bi);
+        }
       }
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16_f32(128, 128, 0, 0);   // S^T, dP^T
       constexpr uint32_t idKV = idesc_bf16_f32(128, 64, 0, 1);   // dV, dK: B MN-major
       constexpr uint32_t idQ = idesc_bf16_f32(128, 64, 1, 1);    // dQ: A and B MN-major
-      const uint32_t sK = smem_u32(smem + OFF_K), sV = smem_u32(smem + OFF_V);
       const uint32_t sDS = smem_u32(smem + OFF_DS);
-      bool ok = mbar_wait(kv_full, 0, ab);
-      for (int it = 0; ok && it < n_it; ++it) {
-        const int slot = it & 1;
-        if (!mbar_wait(&qdo_full[slot], (it >> 1) & 1, ab)) { ok = false; break; }
-        if (it > 0 && !mbar_wait(st_free, (it - 1) & 1, ab)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t sQ = smem_u32(smem + OFF_Q + slot * TILE);
-        const uint32_t sDO = smem_u32(smem + OFF_DO + slot * TILE);
-#pragma unroll
-        for (int k = 0; k < HD / 16; ++k)
-          umma_f16_ss(tmem + COL_S, sdesc_sw128(sK + k * 32, 16, 1024), sdesc_sw128(sQ + k * 32, 16, 1024), idS,
-                      k > 0);
-#pragma unroll
-        for (int k = 0; k < HD / 16; ++k)
-          umma_f16_ss(tmem + COL_DP, sdesc_sw128(sV + k * 32, 16, 1024), sdesc_sw128(sDO + k * 32, 16, 1024), idS,
-                      k > 0);
-        umma_commit(s_full);
-        if (!mbar_wait(ds_full, it & 1, ab)) { ok = false; break; }
-        tc_fence_after();
-        if (p.want_dkdv) {
-#pragma unroll
-          for (int kk = 0; kk < BQ / 16; ++kk) {
-            const uint32_t a_off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_f16_ts(tmem + COL_DV, tmem + COL_PT + kk * 8, sdesc_sw128(sDO + kk * 2048, 8192, 1024), idKV,
-                        (it > 0 || kk > 0) ? 1u : 0u);
-            umma_f16_ss(tmem + COL_DK, sdesc_sw128(sDS + a_off, 16, 1024), sdesc_sw128(sQ + kk * 2048, 8192, 1024),
-                        idKV, (it > 0 || kk > 0) ? 1u : 0u);
-          }
-        }
-        if (p.want_dq) {
-          if (it > 0 && !mbar_wait(dq_free, (it - 1) & 1, ab)) { ok = false; break; }
+      bool ok = true;
+      int g = 0, wi = 0;
+      for (int w = bwd_round_item(0); ok && w < n_items; w = bwd_round_item(++wi)) {
+        int jb, head;
+        bwd_item(p, w, jb, head);
+        const int ks = wi & 1;
+        const uint32_t sK = smem_u32(smem + OFF_K + ks * TILE), sV = smem_u32(smem + OFF_V + ks * TILE);
+        if (!mbar_wait(&kv_full[ks], (wi >> 1) & 1, ab)) break;
+        for (int it = 0; jb + it < p.nq; ++it, ++g) {
+          const int slot = g & 1;
+          if (!mbar_wait(&qdo_full[slot], (g >> 1) & 1, ab)) { ok = false; break; }
+          if (g > 0 && !mbar_wait(st_free, (g - 1) & 1, ab)) { ok = false; break; }
           tc_fence_after();
+          const uint32_t sQ = smem_u32(smem + OFF_Q + slot * TILE);
+          const uint32_t sDO = smem_u32(smem + OFF_DO + slot * TILE);
 #pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk)
-            umma_f16_ss(tmem + COL_DQ, sdesc_sw128(sDS + kk * 2048, 16384, 1024),
-                        sdesc_sw128(sK + kk * 2048, 8192, 1024), idQ, kk > 0 ? 1u : 0u);
-          umma_commit(dq_full);
+          for (int k = 0; k < HD / 16; ++k)
+            umma_f16_ss(tmem + COL_S, sdesc_sw128(sK + k * 32, 16, 1024), sdesc_sw128(sQ + k * 32, 16, 1024), idS,
+                        k > 0);
+#pragma unroll
+          for (int k = 0; k < HD / 16; ++k)
+            umma_f16_ss(tmem + COL_DP, sdesc_sw128(sV + k * 32, 16, 1024), sdesc_sw128(sDO + k * 32, 16, 1024),
+                        idS, k > 0);
+          umma_commit(s_full);
+          if (!mbar_wait(ds_full, g & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+          if (p.want_dkdv) {
+            // the previous item's dV / dK must have left TMEM before they restart
+            if (it == 0 && wi > 0 && !mbar_wait(acc_free, (wi - 1) & 1, ab)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < BQ / 16; ++kk) {
+              const uint32_t a_off = (kk >> 2) * 16384 + (kk & 3) * 32;
+              umma_f16_ts(tmem + COL_DV, tmem + COL_PT + kk * 8, sdesc_sw128(sDO + kk * 2048, 8192, 1024), idKV,
+                          (it > 0 || kk > 0) ? 1u : 0u);
+              umma_f16_ss(tmem + COL_DK, sdesc_sw128(sDS + a_off, 16, 1024),
+                          sdesc_sw128(sQ + kk * 2048, 8192, 1024), idKV, (it > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          if (p.want_dq) {
+            if (g > 0 && !mbar_wait(dq_free, (g - 1) & 1, ab)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < BKV / 16; ++kk)
+              umma_f16_ss(tmem + COL_DQ, sdesc_sw128(sDS + kk * 2048, 16384, 1024),
+                          sdesc_sw128(sK + kk * 2048, 8192, 1024), idQ, kk > 0 ? 1u : 0u);
+            umma_commit(dq_full);
+          }
+          umma_commit(ds_empty);
+          umma_commit(&qdo_empty[slot]);
         }
-        umma_commit(ds_empty);
-        umma_commit(&qdo_empty[slot]);
+        if (!ok) break;
+        umma_commit(&kv_empty[ks]);
+        umma_commit(acc_done);
       }
-      if (ok) umma_commit(acc_done);
     }
   } else if (warp < 10) {
     // ---------------------------------------------------------- P / dS warps
@@ -467,105 +508,117 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const int t = (warp - 2) * 32 + lane;  // loader index: threads 0..127 stage L / D
-    const int kv = jb * BKV + r;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const uint32_t sDS = smem_u32(smem + OFF_DS);
-    const float* Lh = p.L + (long long)head * p.s;
-    const float* Dh = p.D + (long long)head * p.s;
-    float l_next, d_next;
-    {
-      const int qi = jb * BQ + t;
-      l_next = (t < 128 && qi < p.s) ? Lh[qi] * kLog2e : INFINITY;
-      d_next = (t < 128 && qi < p.s) ? Dh[qi] : 0.f;
-    }
-    // On a timeout the loop keeps iterating without work so that all 256
+    // On a timeout the loops keep iterating without work so that all 256
     // threads still meet at every named barrier (a barrier can not time out).
     bool ok = true;
-    for (int it = 0; it < n_it; ++it) {
-      const int i = jb + it, buf = it & 1;
-      if (t < 128) {
-        Lbuf[buf * 128 + t] = l_next;
-        Dbuf[buf * 128 + t] = d_next;
-      }
-      named_bar_sync(1, 256);
-      if (it + 1 < n_it) {
-        const int qi = (i + 1) * BQ + t;
+    int g = 0, wi = 0;
+    for (int w = bwd_round_item(0); w < n_items; w = bwd_round_item(++wi)) {
+      int jb, head;
+      bwd_item(p, w, jb, head);
+      const int bi = head / p.H, hi = head % p.H;
+      const int kv = jb * BKV + r;
+      const float* Lh = p.L + (long long)head * p.s;
+      const float* Dh = p.D + (long long)head * p.s;
+      float l_next, d_next;
+      {
+        const int qi = jb * BQ + t;
         l_next = (t < 128 && qi < p.s) ? Lh[qi] * kLog2e : INFINITY;
         d_next = (t < 128 && qi < p.s) ? Dh[qi] : 0.f;
       }
-      if (ok) ok = mbar_wait_warp(s_full, it & 1, ab);
-      if (ok && it > 0) ok = mbar_wait_warp(ds_empty, (it - 1) & 1, ab);
-      if (!ok) continue;
-      tc_fence_after();
-      const float* Lb = Lbuf + buf * 128;
-      const float* Db = Dbuf + buf * 128;
-      // the causal / sequence-end mask is needed only on the diagonal tile and
-      // on a ragged last query tile (warp-uniform)
-      const bool masked = (i == jb) || ((i + 1) * BQ > p.s);
+      for (int i = jb; i < p.nq; ++i, ++g) {
+        const int buf = g & 1;
+        if (t < 128) {
+          Lbuf[buf * 128 + t] = l_next;
+          Dbuf[buf * 128 + t] = d_next;
+        }
+        named_bar_sync(1, 256);
+        if (i + 1 < p.nq) {
+          const int qi = (i + 1) * BQ + t;
+          l_next = (t < 128 && qi < p.s) ? Lh[qi] * kLog2e : INFINITY;
+          d_next = (t < 128 && qi < p.s) ? Dh[qi] : 0.f;
+        }
+        if (ok) ok = mbar_wait_warp(s_full, g & 1, ab);
+        if (ok && g > 0) ok = mbar_wait_warp(ds_empty, (g - 1) & 1, ab);
+        if (!ok) continue;
+        tc_fence_after();
+        const float* Lb = Lbuf + buf * 128;
+        const float* Db = Dbuf + buf * 128;
+        // the causal / sequence-end mask is needed only on the diagonal tile
+        // and on a ragged last query tile (warp-uniform)
+        const bool masked = (i == jb) || ((i + 1) * BQ > p.s);
 #pragma unroll 1
-      for (int c = 2 * half; c < 2 * half + 2; ++c) {
-        uint32_t us[32], ud[32];
-        tmem_ld32(trow + COL_S + c * 32, us);
-        tmem_ld32(trow + COL_DP + c * 32, ud);
-        float nl[32], dcol[32];  // -L (base 2) and D of the 32 query columns: broadcast vector loads
+        for (int c = 2 * half; c < 2 * half + 2; ++c) {
+          uint32_t us[32], ud[32];
+          tmem_ld32(trow + COL_S + c * 32, us);
+          tmem_ld32(trow + COL_DP + c * 32, ud);
+          float nl[32], dcol[32];  // -L (base 2) and D of the 32 query columns: broadcast vector loads
 #pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          const float4 l4 = reinterpret_cast<const float4*>(Lb + c * 32)[v];
-          const float4 d4 = reinterpret_cast<const float4*>(Db + c * 32)[v];
-          nl[4 * v] = -l4.x; nl[4 * v + 1] = -l4.y; nl[4 * v + 2] = -l4.z; nl[4 * v + 3] = -l4.w;
-          dcol[4 * v] = d4.x; dcol[4 * v + 1] = d4.y; dcol[4 * v + 2] = d4.z; dcol[4 * v + 3] = d4.w;
-        }
-        tmem_wait_ld();
-        float pv[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) pv[e] = ex2_approx(fmaf(__uint_as_float(us[e]), p.sl2, nl[e]));
-        if (masked) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int qg = i * BQ + c * 32 + e;
-            pv[e] = (qg >= kv && qg < p.s) ? pv[e] : 0.f;  // causal (query >= key), in range
+          for (int v = 0; v < 8; ++v) {
+            const float4 l4 = reinterpret_cast<const float4*>(Lb + c * 32)[v];
+            const float4 d4 = reinterpret_cast<const float4*>(Db + c * 32)[v];
+            nl[4 * v] = -l4.x; nl[4 * v + 1] = -l4.y; nl[4 * v + 2] = -l4.z; nl[4 * v + 3] = -l4.w;
+            dcol[4 * v] = d4.x; dcol[4 * v + 1] = d4.y; dcol[4 * v + 2] = d4.z; dcol[4 * v + 3] = d4.w;
           }
-        }
-        uint32_t pp[16], dd[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          pp[e / 2] = pack_bf16x2(pv[e], pv[e + 1]);
-          dd[e / 2] = pack_bf16x2(pv[e] * (__uint_as_float(ud[e]) - dcol[e]),
-                                  pv[e + 1] * (__uint_as_float(ud[e + 1]) - dcol[e + 1]));
-        }
-#pragma unroll
-        for (int v = 0; v < 4; ++v)
-          st_shared_v4(sDS + sw128_off(r, c * 4 + v), dd[4 * v], dd[4 * v + 1], dd[4 * v + 2], dd[4 * v + 3]);
-        // P^T (bf16 pairs) into TMEM: 32 query columns = 16 packed columns
-        tmem_st16(trow + COL_PT + c * 16, pp);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(st_free);
-      fence_proxy_async_smem();
-      mbar_arrive(ds_full);
-    }
-    if (ok && p.want_dkdv && mbar_wait_warp(acc_done, 0, ab)) {
-      tc_fence_after();
-      {
-        const int which = half;  // half 0 writes dV, half 1 writes dK
-        __nv_bfloat16* dst = (which == 0 ? p.dV : p.dK) + bi * p.gs.b + (long long)kv * p.gs.s + hi * p.gs.h;
-        const float mul = (which == 0) ? 1.f : p.scale;
-        const uint32_t col = (which == 0) ? COL_DV : COL_DK;
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t u[32];
-          tmem_ld32(trow + col + c * 32, u);
           tmem_wait_ld();
-          if (kv < p.s) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+          float pv[32];
 #pragma unroll
-            for (int v = 0; v < 4; ++v)
-              d4[v] = make_uint4(pack_bf16x2(__uint_as_float(u[8 * v + 0]) * mul, __uint_as_float(u[8 * v + 1]) * mul),
-                                 pack_bf16x2(__uint_as_float(u[8 * v + 2]) * mul, __uint_as_float(u[8 * v + 3]) * mul),
-                                 pack_bf16x2(__uint_as_float(u[8 * v + 4]) * mul, __uint_as_float(u[8 * v + 5]) * mul),
-                                 pack_bf16x2(__uint_as_float(u[8 * v + 6]) * mul, __uint_as_float(u[8 * v + 7]) * mul));
+          for (int e = 0; e < 32; ++e) pv[e] = ex2_approx(fmaf(__uint_as_float(us[e]), p.sl2, nl[e]));
+          if (masked) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int qg = i * BQ + c * 32 + e;
+              pv[e] = (qg >= kv && qg < p.s) ? pv[e] : 0.f;  // causal (query >= key), in range
+            }
           }
+          uint32_t pp[16], dd[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            pp[e / 2] = pack_bf16x2(pv[e], pv[e + 1]);
+            dd[e / 2] = pack_bf16x2(pv[e] * (__uint_as_float(ud[e]) - dcol[e]),
+                                    pv[e + 1] * (__uint_as_float(ud[e + 1]) - dcol[e + 1]));
+          }
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            st_shared_v4(sDS + sw128_off(r, c * 4 + v), dd[4 * v], dd[4 * v + 1], dd[4 * v + 2], dd[4 * v + 3]);
+          // P^T (bf16 pairs) into TMEM: 32 query columns = 16 packed columns
+          tmem_st16(trow + COL_PT + c * 16, pp);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(st_free);
+        fence_proxy_async_smem();
+        mbar_arrive(ds_full);
+      }
+      if (ok && p.want_dkdv) ok = mbar_wait_warp(acc_done, wi & 1, ab);
+      if (ok && p.want_dkdv) {
+        tc_fence_after();
+        const int which = half;  // half 0 writes dV, half 1 writes dK
+        const uint32_t col = (which == 0) ? COL_DV : COL_DK;
+        uint32_t u0[32], u1[32];
+        tmem_ld32(trow + col, u0);
+        tmem_ld32(trow + col + 32, u1);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(acc_free);  // TMEM columns free for the next item
+        if (kv < p.s) {
+          __nv_bfloat16* dst = (which == 0 ? p.dV : p.dK) + bi * p.gs.b + (long long)kv * p.gs.s + hi * p.gs.h;
+          const float mul = (which == 0) ? 1.f : p.scale;
+          uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            d4[v] = make_uint4(pack_bf16x2(__uint_as_float(u0[8 * v + 0]) * mul, __uint_as_float(u0[8 * v + 1]) * mul),
+                               pack_bf16x2(__uint_as_float(u0[8 * v + 2]) * mul, __uint_as_float(u0[8 * v + 3]) * mul),
+                               pack_bf16x2(__uint_as_float(u0[8 * v + 4]) * mul, __uint_as_float(u0[8 * v + 5]) * mul),
+                               pack_bf16x2(__uint_as_float(u0[8 * v + 6]) * mul, __uint_as_float(u0[8 * v + 7]) * mul));
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            d4[4 + v] =
+                make_uint4(pack_bf16x2(__uint_as_float(u1[8 * v + 0]) * mul, __uint_as_float(u1[8 * v + 1]) * mul),
+                           pack_bf16x2(__uint_as_float(u1[8 * v + 2]) * mul, __uint_as_float(u1[8 * v + 3]) * mul),
+                           pack_bf16x2(__uint_as_float(u1[8 * v + 4]) * mul, __uint_as_float(u1[8 * v + 5]) * mul),
+                           pack_bf16x2(__uint_as_float(u1[8 * v + 6]) * mul, __uint_as_float(u1[8 * v + 7]) * mul));
         }
       }
     }
@@ -578,30 +631,37 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
       const int quarter = warp & 3;
       const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
       uint8_t* stg = smem + OFF_DQS + (warp - 10) * 8192;
-      for (int it = 0; it < n_it; ++it) {
-        const int q0 = (jb + it) * BQ + quarter * 32;
-        if (!mbar_wait_warp(dq_full, it & 1, ab)) break;
-        tc_fence_after();
-        uint32_t u0[32], u1[32];
-        tmem_ld32(trow + COL_DQ, u0);
-        tmem_ld32(trow + COL_DQ + 32, u1);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(dq_free);
-        if (lane == 0) bulk_wait_read_all();  // the previous reduce has read the staging
-        __syncwarp();
-        const uint32_t b0 = smem_u32(stg) + lane * 128;
+      bool ok = true;
+      int g = 0, wi = 0;
+      for (int w = bwd_round_item(0); ok && w < n_items; w = bwd_round_item(++wi)) {
+        int jb, head;
+        bwd_item(p, w, jb, head);
+        for (int i = jb; i < p.nq; ++i, ++g) {
+          const int q0 = i * BQ + quarter * 32;
+          if (!mbar_wait_warp(dq_full, g & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+          uint32_t u0[32], u1[32];
+          tmem_ld32(trow + COL_DQ, u0);
+          tmem_ld32(trow + COL_DQ + 32, u1);
+          tmem_wait_ld();
+          tc_fence_before();
+          mbar_arrive(dq_free);
+          if (lane == 0) bulk_wait_read_all();  // the previous reduce has read the staging
+          __syncwarp();
+          const uint32_t b0 = smem_u32(stg) + lane * 128;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          st_shared_v4(b0 + ((j ^ (lane & 7)) << 4), u0[4 * j], u0[4 * j + 1], u0[4 * j + 2], u0[4 * j + 3]);
-          st_shared_v4(b0 + 4096 + ((j ^ (lane & 7)) << 4), u1[4 * j], u1[4 * j + 1], u1[4 * j + 2], u1[4 * j + 3]);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0 && q0 < p.s) {
-          tma_reduce_add_3d(&tmDQ, stg, 0, q0, head);
-          tma_reduce_add_3d(&tmDQ, stg + 4096, 32, q0, head);
-          bulk_commit();
+          for (int j = 0; j < 8; ++j) {
+            st_shared_v4(b0 + ((j ^ (lane & 7)) << 4), u0[4 * j], u0[4 * j + 1], u0[4 * j + 2], u0[4 * j + 3]);
+            st_shared_v4(b0 + 4096 + ((j ^ (lane & 7)) << 4), u1[4 * j], u1[4 * j + 1], u1[4 * j + 2],
+                         u1[4 * j + 3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && q0 < p.s) {
+            tma_reduce_add_3d(&tmDQ, stg, 0, q0, head);
+            tma_reduce_add_3d(&tmDQ, stg + 4096, 32, q0, head);
+            bulk_commit();
+          }
         }
       }
       if (lane == 0) bulk_wait_all();
@@ -775,7 +835,8 @@ int flash_bwd(const void* Q, const void* K, const void* V, fa::Strides qs, const
   p.want_dkdv = want_dkdv;
   p.err = device_error_word();
   if ((st = set_smem(flash_bwd_kernel, bwd::SMEM))) return st;
-  const long long grid = static_cast<long long>(n) * p.nq;
+  const long long items = static_cast<long long>(n) * p.nq;
+  const long long grid = items < sm_count() ? items : sm_count();
   flash_bwd_kernel<<<static_cast<unsigned>(grid), bwd::kThreads, bwd::SMEM, stream>>>(tq, tk, tv, tdo, tdq, p);
   if ((st = launch_status())) return st;
   if (want_dq) {
