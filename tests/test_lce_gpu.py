@@ -27,15 +27,15 @@ def run(X, W, t, dev, chunk=None):
     Xt = torch.from_numpy(X).to(dev).requires_grad_()
     Wt = torch.from_numpy(W).to(dev).requires_grad_()
     tt = torch.from_numpy(t).to(dev)
-    if chunk:
-        old = CE._LCE_CHUNK
-        CE._LCE_CHUNK = chunk
+    if chunk:  # target vocabulary chunk of the backward (NLEARN_LCE_CHUNK)
+        old = CE._LCE_CHUNK_ENV
+        CE._LCE_CHUNK_ENV = str(chunk)
     try:
         loss = CE.linear_cross_entropy(Xt, Wt, tt)
         loss.backward()
     finally:
         if chunk:
-            CE._LCE_CHUNK = old
+            CE._LCE_CHUNK_ENV = old
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
     return loss.item(), Xt.grad.cpu().numpy(), Wt.grad.cpu().numpy()
