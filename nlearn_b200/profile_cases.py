@@ -42,6 +42,8 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--pad", type=int, default=0, help="extra elements of row pitch for the GEMM operands")
     ap.add_argument("--accum", action="store_true", help="GEMM into an f32 accumulator (weight-gradient form)")
+    ap.add_argument("--epi", default="store", choices=["store", "bias", "bias_gelu", "resid", "dgelu"],
+                    help="fused epilogue of the bf16-output GEMM")
     a = ap.parse_args(argv)
     dev = torch.device("cuda:0")
     torch.manual_seed(0)
@@ -79,9 +81,17 @@ def main(argv=None):
             C = torch.zeros(M, N, device=dev, dtype=torch.float32)
             ms = _time(lambda: gemm_ex(A, B, a_trans=at, b_trans=bt, out=C, epilogue=EPI_ACCUM), a.iters)
         else:
+            from . import _lib as L
             C = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
-            ms = _time(lambda: gemm_ex(A, B, a_trans=at, b_trans=bt, out=C), a.iters)
-        out.update(M=M, N=N, K=K, layout=a.layout, pad=a.pad, accum=a.accum, ms=ms, tflops=2 * M * N * K / ms / 1e9)
+            epi = {"store": L.EPI_STORE, "bias": L.EPI_BIAS, "bias_gelu": L.EPI_BIAS_GELU, "resid": L.EPI_RESID,
+                   "dgelu": L.EPI_DGELU}[a.epi]
+            bias = torch.randn(N, device=dev) if a.epi in ("bias", "bias_gelu", "resid") else None
+            aux = torch.randn(M, N, device=dev).bfloat16() if a.epi in ("bias_gelu", "dgelu") else None
+            resid = torch.randn(M, N, device=dev).bfloat16() if a.epi == "resid" else None
+            ms = _time(lambda: gemm_ex(A, B, a_trans=at, b_trans=bt, out=C, epilogue=epi, bias=bias, aux=aux,
+                                       resid=resid), a.iters)
+        out.update(M=M, N=N, K=K, layout=a.layout, pad=a.pad, accum=a.accum, epi=a.epi, ms=ms,
+                   tflops=2 * M * N * K / ms / 1e9)
     elif a.case in ("attn_fwd", "attn_bwd"):
         from . import attention as A
         n, s = a.heads, a.seq
