@@ -177,6 +177,7 @@ template <typename T, typename TO, int MODE, int kThreads>
 __global__ void __launch_bounds__(kThreads) ce_kernel(const T* logits, long long ld,
                                                       const int* __restrict__ targets, float* loss, float* lse,
                                                       TO* dlogits, long long ldd, int M, int V, float scale) {
+  griddep_sync();
   const int r = blockIdx.x;
   if (r >= M) return;
   const T* row = logits + (long long)r * ld;
@@ -219,7 +220,7 @@ int dispatch(const void* logits, long long ld, int in_dtype, const int* targets,
   constexpr int NT = (MODE == 3) ? 1024 : 512;
   dim3 grid(M), block(NT);
 #define NL_CE_LAUNCH(T, TO)                                                                                    \
-  ce_kernel<T, TO, MODE, NT><<<grid, block, 0, stream>>>(reinterpret_cast<const T*>(logits), ld, targets, loss, \
+  launch_kernel(ce_kernel<T, TO, MODE, NT>, dim3(grid), dim3(block), 0, stream, 1, reinterpret_cast<const T*>(logits), ld, targets, loss, \
                                                          lse, reinterpret_cast<TO*>(dlogits), ldd, M, V, scale)
   if (in_dtype == NL_F32) {
     if (!(MODE & 2) || out_dtype == NL_F32) NL_CE_LAUNCH(float, float);

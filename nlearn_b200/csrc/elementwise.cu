@@ -44,6 +44,7 @@ template <int DV>  // D / 256: vectors of 8 per lane
 __global__ void embed_fwd_kernel(const int* __restrict__ tok, const __nv_bfloat16* __restrict__ wte,
                                  const __nv_bfloat16* __restrict__ wpe, __nv_bfloat16* __restrict__ out, int M,
                                  int S, int D) {
+  griddep_sync();
   const int lane = threadIdx.x & 31;
   for (long long m = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; m < M;
        m += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
@@ -67,6 +68,7 @@ __global__ void embed_fwd_kernel(const int* __restrict__ tok, const __nv_bfloat1
 template <int DV>
 __global__ void embed_bwd_kernel(const int* __restrict__ tok, const float* __restrict__ dx, float* dwte,
                                  float* dwpe, int M, int S, int D) {
+  griddep_sync();
   const int lane = threadIdx.x & 31;
   for (long long m = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; m < M;
        m += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
@@ -89,6 +91,7 @@ __global__ void layernorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const 
                                      const float* __restrict__ b, __nv_bfloat16* __restrict__ y,
                                      float* __restrict__ mean_out, float* __restrict__ rstd_out, int M, int D,
                                      float eps) {
+  griddep_sync();
   const int lane = threadIdx.x & 31;
   // each lane always owns the same 8-column groups: keep gamma / beta in registers
   float gg[DV][8], bb[DV][8];
@@ -145,6 +148,7 @@ __global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const
                                      const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
                                      const float* __restrict__ g, float* dres, __nv_bfloat16* dres_bf, float* dg,
                                      float* db, int M, int D, int accumulate) {
+  griddep_sync();
   const int lane = threadIdx.x & 31;
   float adg[DV][8], adb[DV][8];
 #pragma unroll
@@ -222,6 +226,7 @@ __global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const
 // out[n] (+)= sum_m x[m, n]  for bf16 x [M, N] (N % 8 == 0).  Block = 256
 // threads covering 8*32 = 256 columns x 8 row groups; float atomics per block.
 __global__ void colsum_kernel(const __nv_bfloat16* __restrict__ x, float* out, int M, int N, int rows_per_block) {
+  griddep_sync();
   const int cvec = blockIdx.x * 32 + (threadIdx.x & 31);  // vector of 8 columns
   const int rg = threadIdx.x >> 5;                        // 8 row groups
   if (cvec * 8 >= N) return;
@@ -257,6 +262,7 @@ __global__ void colsum_kernel(const __nv_bfloat16* __restrict__ x, float* out, i
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ shadow, long long n4,
                              const float* __restrict__ hyper, float b1, float b2, float eps, float wd) {
+  griddep_sync();
   const float lr = hyper[0], bc1 = hyper[1], bc2 = hyper[2];
   const float ibc1 = 1.f / bc1, ibc2 = 1.f / bc2;
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
@@ -284,6 +290,7 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
 }
 
 __global__ void cast_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, long long n4) {
+  griddep_sync();
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const float4 a = reinterpret_cast<const float4*>(x)[i];
@@ -311,9 +318,9 @@ extern "C" int nl_embed_fwd(const int* tok, const void* wte, const void* wpe, vo
   auto* o = static_cast<__nv_bfloat16*>(out);
   const int grid = ew::row_grid(M);
   switch (D / 256) {
-    case 1: ew::embed_fwd_kernel<1><<<grid, 256, 0, stream>>>(tok, a, b, o, M, S, D); break;
-    case 2: ew::embed_fwd_kernel<2><<<grid, 256, 0, stream>>>(tok, a, b, o, M, S, D); break;
-    case 4: ew::embed_fwd_kernel<4><<<grid, 256, 0, stream>>>(tok, a, b, o, M, S, D); break;
+    case 1: launch_kernel(ew::embed_fwd_kernel<1>, dim3(grid), dim3(256), 0, stream, 1, tok, a, b, o, M, S, D); break;
+    case 2: launch_kernel(ew::embed_fwd_kernel<2>, dim3(grid), dim3(256), 0, stream, 1, tok, a, b, o, M, S, D); break;
+    case 4: launch_kernel(ew::embed_fwd_kernel<4>, dim3(grid), dim3(256), 0, stream, 1, tok, a, b, o, M, S, D); break;
     default: return NL_ERR_SHAPE;
   }
   return launch_status();
@@ -324,9 +331,9 @@ extern "C" int nl_embed_bwd(const int* tok, const float* dx, float* dwte, float*
   if (M <= 0 || S <= 0 || D % 256) return NL_ERR_SHAPE;
   const int grid = ew::row_grid(M);
   switch (D / 256) {
-    case 1: ew::embed_bwd_kernel<1><<<grid, 256, 0, stream>>>(tok, dx, dwte, dwpe, M, S, D); break;
-    case 2: ew::embed_bwd_kernel<2><<<grid, 256, 0, stream>>>(tok, dx, dwte, dwpe, M, S, D); break;
-    case 4: ew::embed_bwd_kernel<4><<<grid, 256, 0, stream>>>(tok, dx, dwte, dwpe, M, S, D); break;
+    case 1: launch_kernel(ew::embed_bwd_kernel<1>, dim3(grid), dim3(256), 0, stream, 1, tok, dx, dwte, dwpe, M, S, D); break;
+    case 2: launch_kernel(ew::embed_bwd_kernel<2>, dim3(grid), dim3(256), 0, stream, 1, tok, dx, dwte, dwpe, M, S, D); break;
+    case 4: launch_kernel(ew::embed_bwd_kernel<4>, dim3(grid), dim3(256), 0, stream, 1, tok, dx, dwte, dwpe, M, S, D); break;
     default: return NL_ERR_SHAPE;
   }
   return launch_status();
@@ -339,9 +346,9 @@ extern "C" int nl_layernorm_fwd(const void* x, const float* g, const float* b, v
   auto* yo = static_cast<__nv_bfloat16*>(y);
   const int grid = ew::row_grid(M);
   switch (D / 256) {
-    case 1: ew::layernorm_fwd_kernel<1><<<grid, 256, 0, stream>>>(xi, g, b, yo, mean, rstd, M, D, eps); break;
-    case 2: ew::layernorm_fwd_kernel<2><<<grid, 256, 0, stream>>>(xi, g, b, yo, mean, rstd, M, D, eps); break;
-    case 4: ew::layernorm_fwd_kernel<4><<<grid, 256, 0, stream>>>(xi, g, b, yo, mean, rstd, M, D, eps); break;
+    case 1: launch_kernel(ew::layernorm_fwd_kernel<1>, dim3(grid), dim3(256), 0, stream, 1, xi, g, b, yo, mean, rstd, M, D, eps); break;
+    case 2: launch_kernel(ew::layernorm_fwd_kernel<2>, dim3(grid), dim3(256), 0, stream, 1, xi, g, b, yo, mean, rstd, M, D, eps); break;
+    case 4: launch_kernel(ew::layernorm_fwd_kernel<4>, dim3(grid), dim3(256), 0, stream, 1, xi, g, b, yo, mean, rstd, M, D, eps); break;
     default: return NL_ERR_SHAPE;
   }
   return launch_status();
@@ -358,13 +365,13 @@ extern "C" int nl_layernorm_bwd(const void* dy, const void* x, const float* mean
   if (grid > 2 * sm_count()) grid = 2 * sm_count();  // few blocks: cheap gamma/beta atomics
   switch (D / 256) {
     case 1:
-      ew::layernorm_bwd_kernel<1><<<grid, 256, 0, stream>>>(dyi, xi, mean, rstd, g, dres, rb, dg, db, M, D, accumulate);
+      launch_kernel(ew::layernorm_bwd_kernel<1>, dim3(grid), dim3(256), 0, stream, 1, dyi, xi, mean, rstd, g, dres, rb, dg, db, M, D, accumulate);
       break;
     case 2:
-      ew::layernorm_bwd_kernel<2><<<grid, 256, 0, stream>>>(dyi, xi, mean, rstd, g, dres, rb, dg, db, M, D, accumulate);
+      launch_kernel(ew::layernorm_bwd_kernel<2>, dim3(grid), dim3(256), 0, stream, 1, dyi, xi, mean, rstd, g, dres, rb, dg, db, M, D, accumulate);
       break;
     case 4:
-      ew::layernorm_bwd_kernel<4><<<grid, 256, 0, stream>>>(dyi, xi, mean, rstd, g, dres, rb, dg, db, M, D, accumulate);
+      launch_kernel(ew::layernorm_bwd_kernel<4>, dim3(grid), dim3(256), 0, stream, 1, dyi, xi, mean, rstd, g, dres, rb, dg, db, M, D, accumulate);
       break;
     default: return NL_ERR_SHAPE;
   }
@@ -375,7 +382,7 @@ extern "C" int nl_colsum_bf16(const void* x, float* out, int M, int N, cudaStrea
   if (M <= 0 || N <= 0 || N % 8) return NL_ERR_SHAPE;
   const int rows_per_block = 64;
   dim3 grid((N / 8 + 31) / 32, (M + rows_per_block - 1) / rows_per_block);
-  ew::colsum_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), out, M, N, rows_per_block);
+  launch_kernel(ew::colsum_kernel, dim3(grid), dim3(256), 0, stream, 1, static_cast<const __nv_bfloat16*>(x), out, M, N, rows_per_block);
   return launch_status();
 }
 
@@ -386,7 +393,7 @@ extern "C" int nl_adamw_step(float* p, const float* g, float* m, float* v, void*
   long long blocks = (n4 + 255) / 256;
   const long long cap = static_cast<long long>(sm_count()) * 16;
   if (blocks > cap) blocks = cap;
-  ew::adamw_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(p, g, m, v,
+  launch_kernel(ew::adamw_kernel, dim3(static_cast<int>(blocks)), dim3(256), 0, stream, 1, p, g, m, v,
                                                                    static_cast<__nv_bfloat16*>(shadow_bf16), n4,
                                                                    hyper, b1, b2, eps, wd);
   return launch_status();
@@ -398,6 +405,6 @@ extern "C" int nl_cast_bf16(const float* x, void* y, long long n, cudaStream_t s
   long long blocks = (n4 + 255) / 256;
   const long long cap = static_cast<long long>(sm_count()) * 16;
   if (blocks > cap) blocks = cap;
-  ew::cast_bf16_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(x, static_cast<__nv_bfloat16*>(y), n4);
+  launch_kernel(ew::cast_bf16_kernel, dim3(static_cast<int>(blocks)), dim3(256), 0, stream, 1, x, static_cast<__nv_bfloat16*>(y), n4);
   return launch_status();
 }

@@ -146,6 +146,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   Abort ab{abort_flag, p.err};
+  griddep_sync();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -409,6 +410,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   Abort ab{abort_flag, p.err};
+  griddep_sync();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA loads
@@ -681,6 +683,7 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
 __global__ void bwd_preprocess_kernel(const __nv_bfloat16* __restrict__ O, const __nv_bfloat16* __restrict__ dO,
                                       Strides os, int H, int s, float* __restrict__ D, float* __restrict__ dQacc,
                                       long long rows) {
+  griddep_sync();
   const int sub = threadIdx.x & 7;
   for (long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 3; row < rows;
        row += (static_cast<long long>(gridDim.x) * blockDim.x) >> 3) {
@@ -714,6 +717,7 @@ __global__ void bwd_preprocess_kernel(const __nv_bfloat16* __restrict__ O, const
 // (possibly strided) dQ layout.
 __global__ void dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dQ, Strides gs, int H,
                                   int s, float scale, long long n8) {
+  griddep_sync();
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long row = i >> 3, c8 = i & 7;
@@ -781,7 +785,7 @@ int flash_fwd(const void* Q, const void* K, const void* V, fa::Strides qs, void*
   if ((st = set_smem(flash_fwd_kernel, fwd::SMEM))) return st;
   const long long grid = static_cast<long long>(p.n) * p.nq;
   if (grid > 0x7fffffffLL) return NL_ERR_SHAPE;
-  flash_fwd_kernel<<<static_cast<unsigned>(grid), fwd::kThreads, fwd::SMEM, stream>>>(tq, tk, tv, p);
+  launch_kernel(flash_fwd_kernel, dim3(static_cast<unsigned>(grid)), dim3(fwd::kThreads), fwd::SMEM, stream, 1, tq, tk, tv, p);
   return launch_status();
 }
 
@@ -806,8 +810,7 @@ int flash_bwd(const void* Q, const void* K, const void* V, fa::Strides qs, const
   const long long rows = static_cast<long long>(n) * s;
   if (O || want_dq) {
     const long long threads = rows * 8;
-    bwd_preprocess_kernel<<<grid_cap((threads + 255) / 256), 256, 0, stream>>>(
-        reinterpret_cast<const __nv_bfloat16*>(O), reinterpret_cast<const __nv_bfloat16*>(dO), os, H, s, D,
+    launch_kernel(bwd_preprocess_kernel, dim3(grid_cap((threads + 255) / 256)), dim3(256), 0, stream, 1, reinterpret_cast<const __nv_bfloat16*>(O), reinterpret_cast<const __nv_bfloat16*>(dO), os, H, s, D,
         want_dq ? dQacc : nullptr, rows);
     if ((st = launch_status())) return st;
   }
@@ -837,12 +840,11 @@ int flash_bwd(const void* Q, const void* K, const void* V, fa::Strides qs, const
   if ((st = set_smem(flash_bwd_kernel, bwd::SMEM))) return st;
   const long long items = static_cast<long long>(n) * p.nq;
   const long long grid = items < sm_count() ? items : sm_count();
-  flash_bwd_kernel<<<static_cast<unsigned>(grid), bwd::kThreads, bwd::SMEM, stream>>>(tq, tk, tv, tdo, tdq, p);
+  launch_kernel(flash_bwd_kernel, dim3(static_cast<unsigned>(grid)), dim3(bwd::kThreads), bwd::SMEM, stream, 1, tq, tk, tv, tdo, tdq, p);
   if ((st = launch_status())) return st;
   if (want_dq) {
     const long long n8 = rows * HD / 8;
-    dq_convert_kernel<<<grid_cap((n8 + 255) / 256), 256, 0, stream>>>(
-        dQacc, reinterpret_cast<__nv_bfloat16*>(dQ), qs, H, s, p.scale, n8);
+    launch_kernel(dq_convert_kernel, dim3(grid_cap((n8 + 255) / 256)), dim3(256), 0, stream, 1, dQacc, reinterpret_cast<__nv_bfloat16*>(dQ), qs, H, s, p.scale, n8);
     if ((st = launch_status())) return st;
   }
   return NL_OK;

@@ -582,6 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_sync();
   Abort ab{abort_flag, p.err};
 
   if (warp == 0) {
@@ -681,7 +682,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
   }
   const int units = p.tiles_m * p.tiles_n * p.split_k;
   const int grid = units < sm_count() ? units : sm_count();
-  kern<<<grid, kThreads, C::SMEM, stream>>>(ta, tb, tc, tx, p);
+  launch_kernel(kern, dim3(grid), dim3(kThreads), C::SMEM, stream, 1, ta, tb, tc, tx, p);
   return launch_status();
 }
 
@@ -763,6 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();  // barriers of both CTAs initialised before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_sync();
   Abort ab{abort_flag, p.err};
 
   if (warp == 0) {
@@ -870,20 +872,9 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   const int units = p.tiles_m * p.tiles_n * p.split_k;
   const int pairs = sm_count() / 2;
   const int g = units < pairs ? units : pairs;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * g);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = pair::SMEM;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, tx, p) != cudaSuccess) {
+  if (launch_kernel(kern, dim3(2 * g), dim3(kThreads), pair::SMEM, stream, 2, ta, tb, tc, tx, p) != cudaSuccess) {
     cudaGetLastError();
+    count_launch();
     return NL_ERR_LAUNCH;
   }
   return launch_status();

@@ -6,6 +6,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "../../include/nl_ops.h"
 
@@ -127,6 +128,49 @@ inline int launch_status() {
   count_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? NL_OK : NL_ERR_LAUNCH;
+}
+
+// Programmatic dependent launch for every kernel of this library (each one
+// executes griddepcontrol.wait before its first global-memory access), so a
+// kernel's launch and prologue overlap the tail of the one before it on the
+// stream.  NL_PDL=0 turns it off.
+inline bool pdl_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("NL_PDL");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
+// Launch `kern` with the library's launch attributes (PDL, and a cluster
+// dimension when cluster_x > 1).  A failed launch is also the runtime's last
+// error, which the launch_status() that follows every launch reports.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                 int cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (cluster_x > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = cluster_x;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
 }  // namespace nl

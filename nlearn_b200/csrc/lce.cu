@@ -21,6 +21,7 @@
 
 #include "gemm.h"
 #include "host_common.h"
+#include "sm100.cuh"
 
 namespace nl {
 namespace lce {
@@ -40,6 +41,7 @@ __device__ __forceinline__ float ex2f(float x) {
 __global__ void lce_reduce_kernel(const float2* __restrict__ part, const float* __restrict__ tgt_logit,
                                   const int* __restrict__ targets, float* __restrict__ loss, float* __restrict__ lse,
                                   int M, int tiles, int V) {
+  griddep_sync();
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= M) return;
   float m = -INFINITY, s = 0.f;
@@ -103,7 +105,7 @@ extern "C" int nl_lce_fwd(const void* X, int ldx, const void* W, int ldw, const 
                     nullptr, stream, &ex);
   if (st) return st;
   const int tiles = 2 * ((V + lce::kTileN - 1) / lce::kTileN);
-  lce::lce_reduce_kernel<<<(M + 127) / 128, 128, 0, stream>>>(ex.part, ex.tgt_logit, targets, loss, lse, M, tiles,
+  launch_kernel(lce::lce_reduce_kernel, dim3((M + 127) / 128), dim3(128), 0, stream, 1, ex.part, ex.tgt_logit, targets, loss, lse, M, tiles,
                                                                V);
   return launch_status();
 }

@@ -135,6 +135,16 @@ __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* m, const vo
                "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
                : "memory");
 }
+// Programmatic dependent launch: wait until the grids this one depends on have
+// completed and their writes are visible (a no-op for a normal launch), and
+// allow the next grid on the stream to be scheduled.  Every kernel of this
+// library calls both before its first global-memory access.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void griddep_sync() {
+  griddep_wait();
+  griddep_launch();
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // All committed bulk stores of this thread have finished READING shared memory.
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
