@@ -36,26 +36,42 @@ __device__ __forceinline__ float ex2f(float x) {
   return y;
 }
 
-// One thread per row: combine the per-half-tile partials (max in natural units,
-// sum of exp(x - max)), coalesced across rows.
-__global__ void lce_reduce_kernel(const float2* __restrict__ part, const float* __restrict__ tgt_logit,
-                                  const int* __restrict__ targets, float* __restrict__ loss, float* __restrict__ lse,
-                                  int M, int tiles, int V) {
+// Combine the per-half-tile partials (max in natural units, sum of
+// exp(x - max)) of each row: a block takes 32 rows; lane = row (coalesced for
+// a fixed tile), each of the 8 warps walks every 8th tile, and the 8 running
+// (max, sum) pairs of a row are merged through shared memory.
+constexpr int kReduceWarps = 8;
+
+__device__ __forceinline__ void lse_merge(float& m, float& s, float pm, float ps) {
+  if (pm == -INFINITY) return;
+  if (pm > m) {
+    s = s * ex2f((m - pm) * kLog2e) + ps;
+    m = pm;
+  } else {
+    s += ps * ex2f((pm - m) * kLog2e);
+  }
+}
+
+__global__ void __launch_bounds__(32 * kReduceWarps) lce_reduce_kernel(
+    const float2* __restrict__ part, const float* __restrict__ tgt_logit, const int* __restrict__ targets,
+    float* __restrict__ loss, float* __restrict__ lse, int M, int tiles, int V) {
   griddep_sync();
-  const int row = blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= M) return;
+  __shared__ float2 red[kReduceWarps][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int row = blockIdx.x * 32 + lane;
   float m = -INFINITY, s = 0.f;
+  if (row < M) {
 #pragma unroll 4
-  for (int t = 0; t < tiles; ++t) {
-    const float2 p = part[(long long)t * M + row];
-    if (p.x == -INFINITY) continue;
-    if (p.x > m) {
-      s = s * ex2f((m - p.x) * kLog2e) + p.y;
-      m = p.x;
-    } else {
-      s += p.y * ex2f((p.x - m) * kLog2e);
+    for (int t = w; t < tiles; t += kReduceWarps) {
+      const float2 p = part[(long long)t * M + row];
+      lse_merge(m, s, p.x, p.y);
     }
   }
+  red[w][lane] = make_float2(m, s);
+  __syncthreads();
+  if (w != 0 || row >= M) return;
+#pragma unroll
+  for (int k = 1; k < kReduceWarps; ++k) lse_merge(m, s, red[k][lane].x, red[k][lane].y);
   const float l = m + __log2f(s) * kLn2;
   lse[row] = l;
   const int t = targets[row];
@@ -105,8 +121,8 @@ extern "C" int nl_lce_fwd(const void* X, int ldx, const void* W, int ldw, const 
                     nullptr, stream, &ex);
   if (st) return st;
   const int tiles = 2 * ((V + lce::kTileN - 1) / lce::kTileN);
-  launch_kernel(lce::lce_reduce_kernel, dim3((M + 127) / 128), dim3(128), 0, stream, 1, ex.part, ex.tgt_logit, targets, loss, lse, M, tiles,
-                                                               V);
+  launch_kernel(lce::lce_reduce_kernel, dim3((M + 31) / 32), dim3(32 * lce::kReduceWarps), 0, stream, 1, ex.part,
+                ex.tgt_logit, targets, loss, lse, M, tiles, V);
   return launch_status();
 }
 

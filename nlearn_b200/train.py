@@ -204,6 +204,39 @@ class Trainer:
                    tmp)
         os.replace(tmp, path)
 
+    def _named(self, buf: torch.Tensor) -> dict:
+        return {name: self.P.view(buf, name).detach().cpu().numpy() for name, _, _ in self.P.specs}
+
+    def _load_named(self, buf: torch.Tensor, named: dict):
+        for name, shape, _ in self.P.specs:
+            self.P.view(buf, name).copy_(torch.from_numpy(np.asarray(named[name], np.float32).reshape(shape)))
+
+    def save_reference(self, path: str):
+        """Resume state in the reference's pickle format ({params, opt_state,
+        step}, nested numpy trees; nlearn/train.py:74-87)."""
+        from .checkpoint import save_resume_state
+        if self.rank != 0:
+            return
+        save_resume_state(self._named(self.P.master), self._named(self.P.exp_avg), self._named(self.P.exp_avg_sq),
+                          self.opt.t, self.step_idx, self.cfg, path)
+
+    def load_reference(self, path: str) -> bool:
+        """Resume from a reference-format pickle; False when the file is absent
+        (nlearn/train.py:90-96).  The data stream continues at the step count."""
+        from .checkpoint import load_resume_state
+        st = load_resume_state(path, self.cfg)
+        if st is None:
+            return False
+        params, mu, nu, count, step = st
+        self._load_named(self.P.master, params)
+        self._load_named(self.P.exp_avg, mu)
+        self._load_named(self.P.exp_avg_sq, nu)
+        self.P.refresh_shadow()
+        self.opt.t = count
+        self.step_idx = step
+        self.loader.step = step
+        return True
+
     def load(self, path: str):
         state = torch.load(path, map_location="cpu", weights_only=False)
         self.P.load_state_dict({k: v.to(self.device) for k, v in state["params"].items()})

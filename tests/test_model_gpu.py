@@ -80,3 +80,22 @@ def test_checkpoint_resume_reproduces(cuda, tmp_path):
     b.load(ck)
     lb = [b.train_step(*b.loader.next()) for _ in range(3)]
     assert np.allclose(la, lb, rtol=0, atol=2e-3), (la, lb)
+
+
+def test_reference_format_resume_reproduces(cuda, tmp_path):
+    """Resume through the reference's pickle ({params, opt_state, step},
+    nlearn/train.py:74-96) continues the run as the uninterrupted trainer does."""
+    cfg = GPTConfig()
+    tc = TrainConfig(batch=2, seq=128, steps=20, warmup=2)
+    a = Trainer(cfg, tc, cuda)
+    for _ in range(3):
+        a.train_step(*a.loader.next())
+    ck = str(tmp_path / "resume.pkl")
+    a.save_reference(ck)
+    la = [a.train_step(*a.loader.next()) for _ in range(3)]
+    b = Trainer(cfg, tc, cuda)
+    assert not b.load_reference(str(tmp_path / "absent.pkl"))
+    assert b.load_reference(ck)
+    assert b.step_idx == 3 and b.opt.t == a.opt.t - 3
+    lb = [b.train_step(*b.loader.next()) for _ in range(3)]
+    assert np.allclose(la, lb, rtol=0, atol=2e-3), (la, lb)
