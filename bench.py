@@ -12,11 +12,16 @@ all-reduce + AdamW.  For N > 1 run under torchrun (one rank per GPU, NCCL).
 Reported (one JSON line from rank 0):
   value          tokens/s of the whole job, device-timed with CUDA events over
                  exactly K steps (barrier + synchronize on both sides, max over
-                 ranks), token batches already resident in HBM
-  e2e            same metric through the public API (Trainer.train_step: host
-                 token arrays -> pinned H2D copy -> step -> loss read back)
+                 ranks), token batches already resident in HBM.  On one GPU
+                 the steps are replays of one captured CUDA graph of the whole
+                 step (Trainer.capture_step / step_graphed); with N > 1 ranks
+                 they are eager launches.  The eager figure is also reported.
+  e2e            same metric through the public API (Trainer.step_graphed, or
+                 step_on_device for N > 1: host token arrays in pinned memory
+                 -> H2D copy -> step -> loss read back, every step)
   roofline       the LM-head forward GEMM (nl_lce_fwd, 843.2 GFLOP algorithmic
-                 per launch) timed live with CUDA events, vs MEASURED_PEAKS.json
+                 per launch) timed live with CUDA events over the eager timed
+                 region, vs MEASURED_PEAKS.json
   flash_attention  op-level causal attention fwd+bwd TFLOP/s at configs[0]
   cpu_baseline   the CPU oracle step (oracle/model.py) on the host cores
 --impl reference times that CPU implementation alone (rank 0; others exit 0).
@@ -200,7 +205,7 @@ def flash_op_tflops(dev, iters=20):
             "ms_fwd_bwd": c0["ms_fwd_bwd"], "tflops": c0["tflops"], "shapes": out}
 
 
-def long_context(dev, rank, world, steps=5, warmup=3):
+def long_context(dev, rank, world, steps=5, warmup=3, graphs=True):
     """the same model at seq 4096, GLOBAL batch 8 split over the
     ranks (strong scaling; one sequence per rank at 8 GPUs).  Device-timed
     tokens/s of the whole job, max over ranks."""
@@ -214,13 +219,18 @@ def long_context(dev, rank, world, steps=5, warmup=3):
     bat = [tr.device_batch(*tr.loader.next()) for _ in range(warmup + steps)]
     for i in range(warmup):
         tr.step_on_device(*bat[i])
+    step = tr.step_on_device
+    if world == 1 and graphs:
+        tr.capture_step()
+        tr.step_graphed(*bat[0])
+        step = tr.step_graphed
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(warmup, warmup + steps):
-        tr.step_on_device(*bat[i])
+        step(*bat[i])
     e1.record()
     torch.cuda.synchronize()
     t = torch.tensor([e0.elapsed_time(e1)], device=dev)
@@ -232,6 +242,7 @@ def long_context(dev, rank, world, steps=5, warmup=3):
     torch.cuda.empty_cache()
     return {"config": "seq 4096, global batch 8 (configs[4]), strong scaling", "per_rank_batch": per_rank,
             "ms_per_step": ms, "value": tokens / (ms * 1e-3), "unit": UNIT,
+            "timing": "CUDA-graph replay" if (world == 1 and graphs) else "eager launches",
             "mfu": tokens / (ms * 1e-3) * 280.2e6 / (world * peaks()[1] * 1e12)}
 
 
@@ -243,6 +254,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-long", action="store_true", help="skip the seq-4096 long-context measurement")
+    ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of CUDA-graph replay")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank = int(os.environ.get("RANK", "0"))
@@ -306,11 +318,29 @@ def main():
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t)
+    ms_eager = float(t)
     head_avg_ms = statistics.mean(s.elapsed_time(e) for s, e in head_ms)
     M.lce_fwd_raw = orig_fwd
     tokens = BATCH * SEQ * world * args.steps
-    value = tokens / (ms_max * 1e-3)
+    value_eager = tokens / (ms_eager * 1e-3)
+
+    # the same steps replayed from one captured CUDA graph (single rank)
+    graphed = world == 1 and not args.no_graph
+    ms_max, value = ms_eager, value_eager
+    if graphed:
+        per_step = tr.capture_step()
+        for i in range(2):
+            tr.step_graphed(*dbat[i])
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for i in range(args.warmup, nb):
+            loss = tr.step_graphed(*dbat[i])
+        g1.record()
+        barrier()
+        ms_max = g0.elapsed_time(g1)
+        value = tokens / (ms_max * 1e-3)
+        launches = per_step * args.steps
 
     # end to end through the public API: host arrays in, host loss out
     pinned = [(torch.from_numpy(x).pin_memory(), torch.from_numpy(y).pin_memory()) for x, y in host[:args.steps]]
@@ -319,9 +349,12 @@ def main():
     f1 = torch.cuda.Event(enable_timing=True)
     f0.record()
     for x, y in pinned:
-        tok = x.to(dev, non_blocking=True)
-        tgt = y.to(dev, non_blocking=True)
-        lv = float(tr.step_on_device(tok, tgt))   # D2H read of the loss
+        if graphed:
+            lv = float(tr.step_graphed(x, y))   # H2D of the batch into the graph's inputs, D2H of the loss
+        else:
+            tok = x.to(dev, non_blocking=True)
+            tgt = y.to(dev, non_blocking=True)
+            lv = float(tr.step_on_device(tok, tgt))   # D2H read of the loss
     f1.record()
     barrier()
     t2 = torch.tensor([f0.elapsed_time(f1)], device=dev)
@@ -330,7 +363,7 @@ def main():
     e2e_value = tokens / (float(t2) * 1e-3)
 
     flash = flash_op_tflops(dev) if rank == 0 else None
-    longc = long_context(dev, rank, world) if not args.no_long else None
+    longc = long_context(dev, rank, world, graphs=not args.no_graph) if not args.no_long else None
     clk = clocks.stop()
     burst, sustained, hbm, src = peaks()
     achieved = HEAD_GEMM_FLOP / (head_avg_ms * 1e-3) / 1e12
@@ -361,6 +394,9 @@ def main():
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 2 * BATCH * SEQ * 4,
                     "d2h_bytes_per_step": 4},
             "gpu_launches": launches,
+            "timing": {"mode": "CUDA-graph replay of the whole step" if graphed else "eager launches",
+                       "eager_value": value_eager, "eager_ms_per_step": ms_eager / args.steps,
+                       "roofline_from": "the eager timed region (same kernels and shapes)"},
             "roofline": {"bound": "tensor", "kernel": "LM-head forward GEMM (nl_lce_fwd, M16384 N50257 K512)",
                          "achieved": achieved, "peak": sustained, "unit": "TFLOP/s",
                          "frac": achieved / sustained, "peak_source": f"{src} bf16_tflops_sustained",

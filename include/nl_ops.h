@@ -190,6 +190,13 @@ NL_API int nl_colsum_bf16(const void* x, float* out, int M, int N, cudaStream_t 
 NL_API int nl_adamw_step(float* p, const float* g, float* m, float* v, void* shadow_bf16, long long n,
                          const float* hyper, float b1, float b2, float eps, float wd, cudaStream_t stream);
 NL_API int nl_cast_bf16(const float* x, void* y, long long n, cudaStream_t stream);
+/* Advance the optimizer step on the device (for CUDA-graph replay): t =
+ * ++(*step) (device int32), then hyper[0] = warmup-cosine learning rate at
+ * step t-1 (optax.warmup_cosine_decay_schedule(0, peak, warmup, decay_steps,
+ * end), as nlearn/train.py:487-505 builds it), hyper[1] = 1 - b1^t,
+ * hyper[2] = 1 - b2^t.  No reference counterpart (optax runs on the host). */
+NL_API int nl_adamw_schedule(float* hyper, int* step, float peak_lr, int warmup, int decay_steps, float end_lr,
+                             float b1, float b2, cudaStream_t stream);
 
 /* ---------------------------------------------------------------- fused LM-head CE
  * Replaces the jnp-chunked `linear_cross_entropy` (nlearn/kernels/

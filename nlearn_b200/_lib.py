@@ -51,6 +51,7 @@ SIGNATURES: dict[str, list] = {
     "nl_layernorm_bwd": [c_void_p] * 9 + [c_int, c_int, c_int, c_void_p],
     "nl_colsum_bf16": [c_void_p, c_void_p, c_int, c_int, c_void_p],
     "nl_adamw_step": [c_void_p] * 5 + [c_longlong, c_void_p, c_float, c_float, c_float, c_float, c_void_p],
+    "nl_adamw_schedule": [c_void_p, c_void_p, c_float, c_int, c_int, c_float, c_float, c_float, c_void_p],
     "nl_cast_bf16": [c_void_p, c_void_p, c_longlong, c_void_p],
     "nl_lce_workspace_bytes": [c_int, c_int, c_int],
     "nl_lce_fwd": [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t,

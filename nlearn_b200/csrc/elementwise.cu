@@ -289,6 +289,30 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   }
 }
 
+// One thread: the device-side step counter and this step's AdamW scalars.
+__global__ void adamw_schedule_kernel(float* hyper, int* step, float peak, int warmup, int decay_steps, float end,
+                                      float b1, float b2) {
+  griddep_sync();
+  const int t = *step + 1;
+  *step = t;
+  const int s = t - 1;  // the schedule counts from 0
+  float lr;
+  if (warmup > 0 && s < warmup) {
+    lr = peak * static_cast<float>(s) / static_cast<float>(warmup);
+  } else if (decay_steps <= warmup) {
+    lr = end;
+  } else {
+    int k = s - warmup;
+    if (k < 0) k = 0;
+    if (k > decay_steps - warmup) k = decay_steps - warmup;
+    const float frac = static_cast<float>(k) / static_cast<float>(decay_steps - warmup);
+    lr = end + (peak - end) * 0.5f * (1.f + cosf(3.14159265358979f * frac));
+  }
+  hyper[0] = lr;
+  hyper[1] = 1.f - powf(b1, static_cast<float>(t));
+  hyper[2] = 1.f - powf(b2, static_cast<float>(t));
+}
+
 __global__ void cast_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, long long n4) {
   griddep_sync();
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
@@ -396,6 +420,14 @@ extern "C" int nl_adamw_step(float* p, const float* g, float* m, float* v, void*
   launch_kernel(ew::adamw_kernel, dim3(static_cast<int>(blocks)), dim3(256), 0, stream, 1, p, g, m, v,
                                                                    static_cast<__nv_bfloat16*>(shadow_bf16), n4,
                                                                    hyper, b1, b2, eps, wd);
+  return launch_status();
+}
+
+extern "C" int nl_adamw_schedule(float* hyper, int* step, float peak_lr, int warmup, int decay_steps, float end_lr,
+                                 float b1, float b2, cudaStream_t stream) {
+  if (!hyper || !step) return NL_ERR_SHAPE;
+  launch_kernel(ew::adamw_schedule_kernel, dim3(1), dim3(1), 0, stream, 1, hyper, step, peak_lr, warmup,
+                decay_steps, end_lr, b1, b2);
   return launch_status();
 }
 

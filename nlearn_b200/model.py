@@ -277,6 +277,7 @@ class AdamW:
         self.hyper = torch.zeros(3, device=params.device, dtype=torch.float32)
         self._hyper_host = torch.zeros(3, dtype=torch.float32).pin_memory() if params.device.type == "cuda" \
             else torch.zeros(3)
+        self.t_dev = torch.zeros(1, device=params.device, dtype=torch.int32)  # step counter for graph replay
 
     def set_lr(self, lr: float):
         """Stage this step's (lr, bias corrections) into device memory."""
@@ -286,6 +287,17 @@ class AdamW:
         h[1] = 1 - self.b1 ** self.t
         h[2] = 1 - self.b2 ** self.t
         self.hyper.copy_(h, non_blocking=True)
+
+    def advance_on_device(self, peak_lr: float, warmup: int, decay_steps: int, end_lr: float):
+        """set_lr for CUDA-graph replay: a one-thread kernel advances the device
+        step counter and writes the schedule's lr and the bias corrections
+        (the counter must equal ``t`` before the first replay: sync_device_step)."""
+        self.t += 1
+        check(lib.nl_adamw_schedule(ptr(self.hyper), ptr(self.t_dev), peak_lr, warmup, decay_steps, end_lr, self.b1,
+                                    self.b2, stream_handle()), "nl_adamw_schedule")
+
+    def sync_device_step(self):
+        self.t_dev.fill_(self.t)
 
     def step(self):
         self.step_range(0, self.P.numel)

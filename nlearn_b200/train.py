@@ -173,19 +173,66 @@ class Trainer:
         tgt = torch.as_tensor(targets, device=self.device)
         return tok, tgt
 
-    def step_on_device(self, tok: torch.Tensor, tgt: torch.Tensor) -> torch.Tensor:
-        """One optimizer step on device-resident tokens; returns the loss tensor
-        (not synchronised)."""
+    def _step_body(self, tok: torch.Tensor, tgt: torch.Tensor, device_schedule: bool = False) -> torch.Tensor:
         self.P.grad.zero_()
-        self.opt.set_lr(self.lr(self.step_idx))
+        if device_schedule:
+            self.opt.advance_on_device(self.tcfg.peak_lr, self.warmup, self.tcfg.steps, self.tcfg.peak_lr / 10)
+        else:
+            self.opt.set_lr(self.lr(self.step_idx))
         loss, saved = self.model.forward(tok, tgt)
         self.reducer.begin()
         self.model.backward(saved, on_grad_ready=self.reducer.ready)
         self.reducer.finish()
         if self.reducer.optimizer is None:
             self.opt.step()
+        return loss
+
+    def step_on_device(self, tok: torch.Tensor, tgt: torch.Tensor) -> torch.Tensor:
+        """One optimizer step on device-resident tokens; returns the loss tensor
+        (not synchronised)."""
+        loss = self._step_body(tok, tgt)
         self.step_idx += 1
         return loss
+
+    # ------------------------------------------------------------- CUDA graph
+    def capture_step(self) -> int:
+        """Capture one whole training step (zero grads, schedule, forward,
+        backward, AdamW) into a CUDA graph over static token buffers; replay
+        with ``step_graphed``.  One rank only (the multi-rank step, with its
+        NCCL buckets on a side stream, stays eager).  Run a few eager steps
+        first so that every kernel and workspace is initialised.  Returns the
+        number of library kernels in the graph."""
+        if self.world != 1:
+            raise RuntimeError("capture_step: single-rank only")
+        B, S = self.tcfg.batch, self.tcfg.seq
+        self._gtok = torch.zeros(B, S, device=self.device, dtype=torch.int32)
+        self._gtgt = torch.zeros(B, S, device=self.device, dtype=torch.int32)
+        self.opt.sync_device_step()
+        t0 = self.opt.t
+        from . import _lib
+        n0 = _lib.lib.nl_launch_count()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._gloss = self._step_body(self._gtok, self._gtgt, device_schedule=True)
+        self.opt.t = t0  # capture runs nothing; the counter advances per replay
+        self.graph_launches = _lib.lib.nl_launch_count() - n0
+        self._graph = g
+        self._graph_t = t0
+        return self.graph_launches
+
+    def step_graphed(self, tok: torch.Tensor, tgt: torch.Tensor) -> torch.Tensor:
+        """Replay the captured step on this batch (device tensors, or pinned
+        host tensors copied in asynchronously); returns the static loss tensor,
+        valid until the next replay."""
+        if self._graph_t != self.opt.t:  # eager steps or a resume since the last replay
+            self.opt.sync_device_step()
+        self._gtok.copy_(tok, non_blocking=True)
+        self._gtgt.copy_(tgt, non_blocking=True)
+        self._graph.replay()
+        self.opt.t += 1
+        self.step_idx += 1
+        self._graph_t = self.opt.t
+        return self._gloss
 
     def train_step(self, inputs: np.ndarray, targets: np.ndarray) -> float:
         """Host batch in, host loss out (the reference's loop body)."""
