@@ -219,6 +219,30 @@ NL_API int nl_lce_bwd(const void* X, int ldx, const void* W, int ldw, const int*
                       const float* gscale, float grad_mul, float* dX, float* dW, int lddw, int dw_accumulate,
                       void* workspace, size_t ws_bytes, int chunk, int M, int D, int V, cudaStream_t stream);
 
+/* ---------------------------------------------------------------- decode (inference)
+ * Replace the reference's generate loop (nlearn/model.py:417-465: full
+ * recompute per token, jax.random.categorical sampling) with KV-cache decode
+ * steps.  The cache of each layer is its q|k|v rows, [B, S_max, 3*D] bf16
+ * (D = H*64), the layout of the prefill's qkv GEMM output.  `pos` is the
+ * current position in device memory (int32), read by every kernel of a step
+ * and advanced by nl_decode_advance, so a step can be replayed from a graph. */
+/* x[b] = wte[tok[b]] + wpe[*pos]  (bf16 tables, bf16 out [B, D]). */
+NL_API int nl_decode_embed(const int* tok, const int* pos, const void* wte, const void* wpe, void* x, int B, int D,
+                           cudaStream_t stream);
+NL_API size_t nl_decode_workspace_bytes(int B, int H, int S_max);
+/* o[b, h] = softmax(q k^T / sqrt(d)) v over positions 0..*pos of head h, with
+ * q|k|v of position *pos taken from qkv_new [B, 3D] and its k|v row written
+ * into the cache.  d == 64.  Workspace: nl_decode_workspace_bytes, zeroed
+ * once before first use. */
+NL_API int nl_decode_attention(const void* qkv_new, void* cache, void* o, const int* pos, void* workspace,
+                               size_t ws_bytes, int B, int H, int S_max, int d, cudaStream_t stream);
+/* tok[b] = argmax_j(logits[b, j] / T + Gumbel(seed, *pos, b, j)) for T > 0,
+ * argmax_j logits[b, j] for T <= 0; also out[b, *pos + 1] = tok[b] when out
+ * is non-NULL. */
+NL_API int nl_sample_tokens(const float* logits, long long ldl, int V, float temperature, unsigned long long seed,
+                            const int* pos, int* tok, int* out, long long ldo, int B, cudaStream_t stream);
+NL_API int nl_decode_advance(int* pos, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

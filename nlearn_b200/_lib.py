@@ -12,7 +12,7 @@ needs it raises, naming the build command.
 from __future__ import annotations
 
 import ctypes
-from ctypes import c_float, c_int, c_longlong, c_void_p
+from ctypes import c_float, c_int, c_longlong, c_size_t, c_ulonglong, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().with_name("libnl_ops.so")
@@ -52,6 +52,13 @@ SIGNATURES: dict[str, list] = {
     "nl_colsum_bf16": [c_void_p, c_void_p, c_int, c_int, c_void_p],
     "nl_adamw_step": [c_void_p] * 5 + [c_longlong, c_void_p, c_float, c_float, c_float, c_float, c_void_p],
     "nl_adamw_schedule": [c_void_p, c_void_p, c_float, c_int, c_int, c_float, c_float, c_float, c_void_p],
+    "nl_decode_embed": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p],
+    "nl_decode_workspace_bytes": [c_int, c_int, c_int],
+    "nl_decode_attention": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_int, c_int, c_int, c_int,
+                            c_void_p],
+    "nl_sample_tokens": [c_void_p, c_longlong, c_int, c_float, c_ulonglong, c_void_p, c_void_p, c_void_p,
+                         c_longlong, c_int, c_void_p],
+    "nl_decode_advance": [c_void_p, c_void_p],
     "nl_cast_bf16": [c_void_p, c_void_p, c_longlong, c_void_p],
     "nl_lce_workspace_bytes": [c_int, c_int, c_int],
     "nl_lce_fwd": [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t,
@@ -60,7 +67,8 @@ SIGNATURES: dict[str, list] = {
                    c_int, c_int, c_void_p, ctypes.c_size_t, c_int, c_int, c_int, c_int, c_void_p],
 }
 _RESTYPE = {"nl_version": ctypes.c_char_p, "nl_launch_count": c_longlong,
-            "nl_flash_attention_bwd_noalloc_max_rows": c_longlong, "nl_lce_workspace_bytes": ctypes.c_size_t}
+            "nl_flash_attention_bwd_noalloc_max_rows": c_longlong, "nl_lce_workspace_bytes": ctypes.c_size_t,
+            "nl_decode_workspace_bytes": ctypes.c_size_t}
 
 
 class NlError(RuntimeError):

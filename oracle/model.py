@@ -32,6 +32,12 @@ class OracleGPT:
         self.L, self.H, self.V, self.eps = n_layers, n_heads, vocab, eps
 
     def loss(self, tok: torch.Tensor, tgt: torch.Tensor) -> torch.Tensor:
+        logits = self.logits(tok)
+        return F.cross_entropy(logits.reshape(-1, self.V), tgt.reshape(-1).long())
+
+    def logits(self, tok: torch.Tensor) -> torch.Tensor:
+        """[B, S] tokens -> [B, S, V] f32 logits (the model forward of
+        nlearn/model.py:361-398 at the BASELINE architecture)."""
         p, H = self.p, self.H
         B, S = tok.shape
         D = p["wte"].shape[1]
@@ -50,8 +56,7 @@ class OracleGPT:
             u = F.gelu(h @ p[q + "w1"] + p[q + "b1"], approximate="tanh")
             x = x + u @ p[q + "w2"] + p[q + "b2"]
         h = F.layer_norm(x, (D,), p["lnf.g"], p["lnf.b"], self.eps)
-        logits = h @ p["head.w"][:, :self.V]
-        return F.cross_entropy(logits.reshape(-1, self.V), tgt.reshape(-1).long())
+        return h @ p["head.w"][:, :self.V]
 
     def grads(self):
         return {k: (v.grad if v.grad is not None else torch.zeros_like(v)) for k, v in self.p.items()}
