@@ -23,6 +23,8 @@ Reported (one JSON line from rank 0):
                  per launch) timed live with CUDA events over the eager timed
                  region, vs MEASURED_PEAKS.json
   flash_attention  op-level causal attention fwd+bwd TFLOP/s at configs[0]
+  decode         inference: graph-replayed KV-cache decode steps, tokens/s at
+                 batch 1 and 32 (not part of the headline metric)
   cpu_baseline   the CPU oracle step (oracle/model.py) on the host cores
 --impl reference times that CPU implementation alone (rank 0; others exit 0).
 """
@@ -205,6 +207,36 @@ def flash_op_tflops(dev, iters=20):
             "ms_fwd_bwd": c0["ms_fwd_bwd"], "tflops": c0["tflops"], "shapes": out}
 
 
+def decode_rate(dev, P, cfg, batch: int, prompt_len: int = 64, steps: int = 128):
+    """Inference: tokens/s of graph-replayed KV-cache decode steps after a
+    prompt prefill (nlearn_b200.generate.Decoder), CUDA-event timed.  At batch
+    1 a step reads every bf16 weight once, so `weight_gbs` is that traffic
+    divided by the step time (HBM-bound kernel family)."""
+    import numpy as np
+    import torch
+    from nlearn_b200.generate import Decoder
+    dec = Decoder(P, cfg, batch=batch)
+    prompt = np.random.default_rng(0).integers(0, cfg.vocab, (batch, prompt_len)).astype(np.int32)
+    dec.prefill(torch.from_numpy(prompt).to(dev), 0, 1.0)
+    dec.step(0, 1.0)
+    dec.capture(0, 1.0)
+    for _ in range(3):
+        dec._graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        dec._graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    wbytes = sum(int(np.prod(shape)) for name, shape, _ in P.specs if len(shape) == 2 and name not in ("wte", "wpe")) * 2
+    del dec
+    torch.cuda.empty_cache()
+    return {"batch": batch, "prompt": prompt_len, "ms_per_token_step": ms, "tokens_per_s": batch / (ms * 1e-3),
+            "weight_gbs": wbytes / (ms * 1e-3) / 1e9}
+
+
 def long_context(dev, rank, world, steps=5, warmup=3, graphs=True):
     """the same model at seq 4096, GLOBAL batch 8 split over the
     ranks (strong scaling; one sequence per rank at 8 GPUs).  Device-timed
@@ -363,6 +395,7 @@ def main():
     e2e_value = tokens / (float(t2) * 1e-3)
 
     flash = flash_op_tflops(dev) if rank == 0 else None
+    decode = [decode_rate(dev, tr.P, cfg, b) for b in (1, 32)] if rank == 0 else None
     longc = long_context(dev, rank, world, graphs=not args.no_graph) if not args.no_long else None
     clk = clocks.stop()
     burst, sustained, hbm, src = peaks()
@@ -402,6 +435,7 @@ def main():
                          "frac": achieved / sustained, "peak_source": f"{src} bf16_tflops_sustained",
                          "traffic": traffic, "avg_launch_ms": head_avg_ms},
             "flash_attention": flash,
+            "decode": decode,
             "long_context": longc,
             "clocks": clk,
             "cpu_baseline": cpu,
