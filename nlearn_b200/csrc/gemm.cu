@@ -69,11 +69,6 @@ struct Cfg {
   static constexpr int SMEM = STAGES * STAGE_BYTES + kStagingBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
-__device__ __forceinline__ float tanh_approx(float u) {
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
-  return t;
-}
 // GELU, tanh form (the BASELINE model's FFN activation) and its derivative.
 __device__ __forceinline__ float gelu_tanh(float a) {
   const float t = tanh_approx(0.7978845608028654f * (a + 0.044715f * a * a * a));
@@ -901,6 +896,11 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
   if (K == 0) {
     if (epi == NL_EPI_ACCUM) return NL_OK;
     return NL_ERR_SHAPE;
+  }
+  if (ex == nullptr && M <= 8) {
+    const int st = gemv_run(A, lda, a_trans, B, ldb, b_trans, Cp, ldc, c_dtype, M, N, K, alpha, epi, bias, aux,
+                            resid, stream);
+    if (st != -100) return st;
   }
   Params p{};
   p.M = M;

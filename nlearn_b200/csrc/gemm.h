@@ -23,4 +23,11 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
              long long ldc, int c_dtype, int M, int N, int K, float alpha, int epi, const float* bias, void* aux,
              const void* resid, cudaStream_t stream, const GemmExtra* ex);
 
+// Small-M path (M <= 8, A and B row-major, store / accumulate / bias /
+// bias+GELU / residual epilogues): launches and returns a status, or -100 when
+// the shape is not one it takes.  gemm_run tries it first.
+int gemv_run(const void* A, long long lda, int a_trans, const void* B, long long ldb, int b_trans, void* C,
+             long long ldc, int c_dtype, int M, int N, int K, float alpha, int epi, const float* bias, void* aux,
+             const void* resid, cudaStream_t stream);
+
 }  // namespace nl

@@ -90,3 +90,38 @@ def test_gemm_autograd_and_linear(cuda):
     y = linear(x, W)
     assert y.dtype == torch.bfloat16 and y.shape == (4, 64, 1536)
     assert _rel(y, x.float() @ W.float()) < 1e-2
+
+
+GEMV_SHAPES = [(1, 512, 512), (3, 1536, 512), (8, 2048, 512), (5, 512, 2048), (2, 200, 72), (7, 64, 8),
+               (1, 50257, 512), (4, 4096, 4096)]
+
+
+@pytest.mark.parametrize("mnk", GEMV_SHAPES)
+def test_small_m_gemv_path(cuda, mnk):
+    """M <= 8 with row-major operands takes the cluster GEMV kernel (the decode
+    step's products); every epilogue it serves against an fp32 reference."""
+    M, N, K = mnk
+    Np = (N + 63) // 64 * 64                      # padded row pitch (the LM head's W)
+    A = _mk((M, K), 1.0, cuda, 11)
+    Bfull = _mk((K, Np), 0.5, cuda, 12)
+    B = Bfull[:, :N]
+    ref = A.float() @ B.float()
+    C = gemm_ex(A, B)                              # f32 store
+    assert _rel(C, ref) < 1e-5
+    bias = torch.randn(N, device=cuda)
+    Cb = gemm_ex(A, B, out_dtype=torch.bfloat16, epilogue=_lib.EPI_BIAS, bias=bias)
+    assert _rel(Cb, ref + bias) < 1e-2
+    resid = torch.randn(M, N, device=cuda).bfloat16()
+    Cr = gemm_ex(A, B, out_dtype=torch.bfloat16, epilogue=_lib.EPI_RESID, bias=bias, resid=resid)
+    assert _rel(Cr, ref + bias + resid.float()) < 1e-2
+    aux = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    Cg = gemm_ex(A, B, out_dtype=torch.bfloat16, epilogue=_lib.EPI_BIAS_GELU, bias=bias, aux=aux)
+    pre = ref + bias
+    assert _rel(aux, pre) < 1e-2
+    assert _rel(Cg, torch.nn.functional.gelu(pre, approximate="tanh")) < 1e-2
+    acc = torch.randn(M, N, device=cuda)
+    want = acc + 2.0 * ref
+    gemm_ex(A, B, out=acc, epilogue=_lib.EPI_ACCUM, alpha=2.0)
+    assert _rel(acc, want) < 1e-5
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
