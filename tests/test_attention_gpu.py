@@ -69,7 +69,10 @@ def test_golden_flash_fwd_tiled(cuda):
     assert nrel(O, g["O"]) < 2e-2
 
 
-@pytest.mark.parametrize("n,s", [(32, 512), (2, 300), (3, 1), (4, 129), (2, 1024)])
+# (300, 256): 600 backward work items, several snake-order rounds over the
+# persistent CTAs; (2, 4096): the long-context length; (5, 777): ragged tiles
+@pytest.mark.parametrize("n,s", [(32, 512), (2, 300), (3, 1), (4, 129), (2, 1024), (300, 256), (2, 4096),
+                                 (5, 777)])
 def test_shapes(cuda, n, s):
     rng = np.random.default_rng(n * 1000 + s)
     mk = lambda: rng.standard_normal((n, s, 64)).astype(np.float32)
