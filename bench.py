@@ -287,6 +287,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-long", action="store_true", help="skip the seq-4096 long-context measurement")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of CUDA-graph replay")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the attention and decode microbenchmarks (for a kernel launch list)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank = int(os.environ.get("RANK", "0"))
@@ -394,8 +396,9 @@ def main():
         dist.all_reduce(t2, op=dist.ReduceOp.MAX)
     e2e_value = tokens / (float(t2) * 1e-3)
 
-    flash = flash_op_tflops(dev) if rank == 0 else None
-    decode = [decode_rate(dev, tr.P, cfg, b) for b in (1, 32)] if rank == 0 else None
+    extras = rank == 0 and not args.no_extras
+    flash = flash_op_tflops(dev) if extras else None
+    decode = [decode_rate(dev, tr.P, cfg, b) for b in (1, 32)] if extras else None
     longc = long_context(dev, rank, world, graphs=not args.no_graph) if not args.no_long else None
     clk = clocks.stop()
     burst, sustained, hbm, src = peaks()
