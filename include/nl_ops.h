@@ -242,6 +242,15 @@ NL_API int nl_decode_attention(const void* qkv_new, void* cache, void* o, const 
 NL_API int nl_sample_tokens(const float* logits, long long ldl, int V, float temperature, unsigned long long seed,
                             const int* pos, int* tok, int* out, long long ldo, int B, cudaStream_t stream);
 NL_API int nl_decode_advance(int* pos, cudaStream_t stream);
+/* C[M, N] = LayerNorm(x)[M, K] . W[K, N] with the nl_gemm_ex epilogues
+ * (STORE / ACCUM / BIAS / BIAS_GELU / RESID), the LayerNorm (gamma, beta over
+ * K, eps) applied while the small-M kernel stages x; M <= 8, x and W
+ * row-major.  Returns NL_ERR_SHAPE for shapes it does not take (the caller
+ * then runs nl_layernorm_fwd + nl_gemm_ex).  No reference counterpart (a
+ * decode-step fusion). */
+NL_API int nl_linear_ln_small(const void* x, long long ldx, const float* gamma, const float* beta, float eps,
+                              const void* W, long long ldw, void* C, long long ldc, int c_dtype, int M, int N, int K,
+                              int epilogue, const float* bias, void* aux, const void* resid, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -59,6 +59,8 @@ SIGNATURES: dict[str, list] = {
     "nl_sample_tokens": [c_void_p, c_longlong, c_int, c_float, c_ulonglong, c_void_p, c_void_p, c_void_p,
                          c_longlong, c_int, c_void_p],
     "nl_decode_advance": [c_void_p, c_void_p],
+    "nl_linear_ln_small": [c_void_p, c_longlong, c_void_p, c_void_p, c_float, c_void_p, c_longlong, c_void_p,
+                           c_longlong, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
     "nl_cast_bf16": [c_void_p, c_void_p, c_longlong, c_void_p],
     "nl_lce_workspace_bytes": [c_int, c_int, c_int],
     "nl_lce_fwd": [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t,

@@ -28,6 +28,7 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
 // the shape is not one it takes.  gemm_run tries it first.
 int gemv_run(const void* A, long long lda, int a_trans, const void* B, long long ldb, int b_trans, void* C,
              long long ldc, int c_dtype, int M, int N, int K, float alpha, int epi, const float* bias, void* aux,
-             const void* resid, cudaStream_t stream);
+             const void* resid, cudaStream_t stream, const float* ln_g = nullptr, const float* ln_b = nullptr,
+             float ln_eps = 0.f);
 
 }  // namespace nl

@@ -44,6 +44,9 @@ struct Params {
   __nv_bfloat16* aux;
   const void* resid;
   int M, N, K, kslice;
+  const float* ln_g;  // non-null: A is LayerNorm(A) (gamma, beta over K), as the LN kernel rounds it to bf16
+  const float* ln_b;
+  float ln_eps;
 };
 
 __device__ __forceinline__ float gelu(float a) {
@@ -70,9 +73,41 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(Params p) {
   const int kend = min(p.K, kbeg + p.kslice);
   const int nk = kend > kbeg ? kend - kbeg : 0;
 
+  __shared__ float stat[MM][2];
+  if (p.ln_g) {  // per-row mean / rstd over the whole K (two passes), one warp per row
+    for (int m = warp; m < MM; m += kWarps) {
+      float s1 = 0.f;
+      if (m < p.M)
+        for (int k = lane; k < p.K; k += 32) s1 += __bfloat162float(p.A[m * p.lda + k]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      const float mean = s1 / p.K;
+      float s2 = 0.f;
+      if (m < p.M)
+        for (int k = lane; k < p.K; k += 32) {
+          const float d = __bfloat162float(p.A[m * p.lda + k]) - mean;
+          s2 += d * d;
+        }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      if (lane == 0) {
+        stat[m][0] = mean;
+        stat[m][1] = rsqrtf(s2 / p.K + p.ln_eps);
+      }
+    }
+    __syncthreads();
+  }
   for (int i = tid; i < MM * p.kslice; i += kThreads) {
     const int m = i / p.kslice, k = i - m * p.kslice;
-    xs[m][k] = (m < p.M && k < nk) ? __bfloat162float(p.A[m * p.lda + kbeg + k]) : 0.f;
+    float v = 0.f;
+    if (m < p.M && k < nk) {
+      v = __bfloat162float(p.A[m * p.lda + kbeg + k]);
+      if (p.ln_g) {
+        const int kk = kbeg + k;
+        v = __bfloat162float(__float2bfloat16_rn((v - stat[m][0]) * stat[m][1] * p.ln_g[kk] + p.ln_b[kk]));
+      }
+    }
+    xs[m][k] = v;
   }
   __syncthreads();
 
@@ -160,7 +195,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(Params p) {
 // not one the small-M kernel takes (the caller then uses the tcgen05 GEMM).
 int gemv_run(const void* A, long long lda, int a_trans, const void* B, long long ldb, int b_trans, void* C,
              long long ldc, int c_dtype, int M, int N, int K, float alpha, int epi, const float* bias, void* aux,
-             const void* resid, cudaStream_t stream) {
+             const void* resid, cudaStream_t stream, const float* ln_g, const float* ln_b, float ln_eps) {
   static int enabled = -1;
   if (enabled < 0) {
     const char* e = getenv("NL_GEMV");
@@ -200,6 +235,9 @@ int gemv_run(const void* A, long long lda, int a_trans, const void* B, long long
   p.N = N;
   p.K = K;
   p.kslice = (K + ks - 1) / ks;
+  p.ln_g = ln_g;
+  p.ln_b = ln_b;
+  p.ln_eps = ln_eps;
   const dim3 grid(ks, ncb);
   cudaError_t e;
   if (M == 1) e = launch_kernel(gv::gemv_kernel<1>, grid, dim3(gv::kThreads), 0, stream, ks, p);
@@ -211,3 +249,18 @@ int gemv_run(const void* A, long long lda, int a_trans, const void* B, long long
 }
 
 }  // namespace nl
+
+using namespace nl;
+
+extern "C" int nl_linear_ln_small(const void* x, long long ldx, const float* gamma, const float* beta, float eps,
+                                  const void* W, long long ldw, void* C, long long ldc, int c_dtype, int M, int N,
+                                  int K, int epilogue, const float* bias, void* aux, const void* resid,
+                                  cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || !gamma || !beta) return NL_ERR_SHAPE;
+  if (c_dtype != NL_F32 && c_dtype != NL_BF16) return NL_ERR_DTYPE;
+  if (epilogue == NL_EPI_BIAS_GELU && (c_dtype != NL_BF16 || aux == nullptr)) return NL_ERR_DTYPE;
+  if (epilogue == NL_EPI_ACCUM && c_dtype != NL_F32) return NL_ERR_DTYPE;
+  const int st = gemv_run(x, ldx, 0, W, ldw, 0, C, ldc, c_dtype, M, N, K, 1.f, epilogue, bias, aux, resid, stream,
+                          gamma, beta, eps);
+  return st == -100 ? NL_ERR_SHAPE : st;
+}

@@ -9,10 +9,13 @@ new token (model.py:417-447); here the prompt is run once through the
 training kernels (flash forward, fused-epilogue GEMMs), every layer's q|k|v
 rows are kept as the KV cache, and each further token is one decode step:
 
-    embed(tok, pos) -> per layer: LN, qkv GEMM (M = batch), decode attention
-    (appends k|v at pos), proj GEMM + residual, LN, FFN up + bias + GELU,
-    FFN down + bias + residual -> final LN -> LM-head GEMM (f32 logits)
+    embed(tok, pos) -> per layer: LN + qkv GEMM (M = batch), decode attention
+    (appends k|v at pos), proj GEMM + residual, LN + FFN up + bias + GELU,
+    FFN down + bias + residual -> final LN + LM-head GEMM (f32 logits)
     -> sampler -> pos += 1
+
+(each "LN + GEMM" is one kernel at batch <= 8: the small-M GEMM applies the
+LayerNorm while staging its A operand).
 
 The position lives in device memory, so one decode step is captured into a
 CUDA graph once and replayed per token.  The random stream (seed, position,
@@ -56,6 +59,7 @@ class Decoder:
         self.ws = torch.zeros(nbytes, device=dev, dtype=torch.uint8)
         self._graph = None
         self._graph_key = None
+        self._fuse_ln = True  # LayerNorm folded into the small-M GEMM (batch <= 8)
 
     # ------------------------------------------------------------------ pieces
     def _ln(self, x, y, g, b, M):
@@ -67,6 +71,10 @@ class Decoder:
     def _head_and_sample(self, hf_rows, seed: int, temperature: float):
         V = self.cfg.vocab
         gemm_ex(hf_rows, self.P.p("head.w")[:, :V], out=self.logits[:, :V])
+        self._sample(seed, temperature)
+
+    def _sample(self, seed: int, temperature: float):
+        V = self.cfg.vocab
         check(lib.nl_sample_tokens(ptr(self.logits), self.logits.stride(0), V, float(temperature), int(seed),
                                    ptr(self.pos), ptr(self.tok), ptr(self.out), self.out.stride(0), self.B,
                                    stream_handle()), "nl_sample_tokens")
@@ -108,29 +116,43 @@ class Decoder:
         self.pos.fill_(Pl - 1)
         self._head_and_sample(h.view(B, Pl, D)[:, -1], seed, temperature)
 
+    def _ln_linear(self, x, g, b, W, out, epilogue=_lib.EPI_STORE, bias=None, aux=None):
+        """out = LayerNorm(x) . W (+ epilogue): one fused small-M kernel when the
+        shape allows (batch <= 8), else LayerNorm then the GEMM."""
+        if self._fuse_ln:
+            dt = _lib.F32 if out.dtype == torch.float32 else _lib.BF16
+            st = lib.nl_linear_ln_small(ptr(x), x.stride(0), ptr(g), ptr(b), self.cfg.ln_eps, ptr(W), W.stride(0),
+                                        ptr(out), out.stride(0), dt, out.shape[0], out.shape[1], W.shape[0],
+                                        epilogue, ptr(bias), ptr(aux), None, stream_handle())
+            if st == 0:
+                return
+            if st != -1:  # anything but NL_ERR_SHAPE ("not a shape the fused kernel takes") is an error
+                check(st, "nl_linear_ln_small")
+            self._fuse_ln = False
+        self._ln(x, self.h, g, b, self.B)
+        gemm_ex(self.h, W, out=out, epilogue=epilogue, bias=bias, aux=aux)
+
     def step(self, seed: int, temperature: float):
         """One decode step: the token in ``tok`` at position ``pos``."""
         cfg, P = self.cfg, self.P
-        D, H = cfg.d_model, cfg.n_heads
+        D, H, V = cfg.d_model, cfg.n_heads, cfg.vocab
         check(lib.nl_decode_embed(ptr(self.tok), ptr(self.pos), ptr(P.p("wte")), ptr(P.p("wpe")), ptr(self.x),
                                   self.B, D, stream_handle()), "nl_decode_embed")
         x = self.x
         for layer in range(cfg.n_layers):
             pre = f"blocks.{layer}."
-            self._ln(x, self.h, P.f(pre + "ln1.g"), P.f(pre + "ln1.b"), self.B)
-            gemm_ex(self.h, P.p(pre + "wqkv"), out=self.qkv)
+            self._ln_linear(x, P.f(pre + "ln1.g"), P.f(pre + "ln1.b"), P.p(pre + "wqkv"), self.qkv)
             check(lib.nl_decode_attention(ptr(self.qkv), ptr(self.cache[layer]), ptr(self.o), ptr(self.pos),
                                           ptr(self.ws), self.ws.numel(), self.B, H, self.S, 64, stream_handle()),
                   "nl_decode_attention")
             gemm_ex(self.o, P.p(pre + "wo"), out=self.x2, epilogue=_lib.EPI_RESID, resid=x)
-            self._ln(self.x2, self.h, P.f(pre + "ln2.g"), P.f(pre + "ln2.b"), self.B)
-            gemm_ex(self.h, P.p(pre + "w1"), out=self.u, epilogue=_lib.EPI_BIAS_GELU, bias=P.f(pre + "b1"),
-                    aux=self.a)
+            self._ln_linear(self.x2, P.f(pre + "ln2.g"), P.f(pre + "ln2.b"), P.p(pre + "w1"), self.u,
+                            epilogue=_lib.EPI_BIAS_GELU, bias=P.f(pre + "b1"), aux=self.a)
             gemm_ex(self.u, P.p(pre + "w2"), out=self.x3, epilogue=_lib.EPI_RESID, bias=P.f(pre + "b2"),
                     resid=self.x2)
             x = self.x3
-        self._ln(x, self.h, P.f("lnf.g"), P.f("lnf.b"), self.B)
-        self._head_and_sample(self.h, seed, temperature)
+        self._ln_linear(x, P.f("lnf.g"), P.f("lnf.b"), P.p("head.w")[:, :V], self.logits[:, :V])
+        self._sample(seed, temperature)
 
     def capture(self, seed: int, temperature: float):
         g = torch.cuda.CUDAGraph()

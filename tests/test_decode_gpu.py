@@ -138,3 +138,50 @@ def test_generate_entry_point_greedy_and_trim(cuda):
     again = generate(P, prompt, 8, seed=99, temperature=0.0, cfg=cfg)  # greedy ignores the seed
     np.testing.assert_array_equal(out, again)
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1536, 512), (3, 2048, 512), (8, 50257, 512), (2, 200, 72)])
+def test_linear_ln_small(cuda, M, N, K):
+    """LayerNorm folded into the small-M GEMM's A staging vs LayerNorm (rounded
+    to bf16, as the LN kernel writes it) followed by the product."""
+    g = torch.Generator(device="cpu").manual_seed(M * N + K)
+    x = (torch.randn(M, K, generator=g) * 3 + 1).bfloat16().to(cuda)
+    gamma = (torch.rand(K, generator=g) + 0.5).to(cuda)
+    beta = torch.randn(K, generator=g).to(cuda)
+    Np = (N + 63) // 64 * 64
+    W = (torch.randn(K, Np, generator=g) * 0.05).bfloat16().to(cuda)[:, :N]
+    h = torch.nn.functional.layer_norm(x.float(), (K,), gamma, beta, 1e-5).bfloat16().float()
+    ref = h @ W.float()
+    bias = torch.randn(N, device=cuda)
+
+    def run(out, epi, b=None, aux=None, expect=0):
+        dt = _lib.F32 if out.dtype == torch.float32 else _lib.BF16
+        st = lib.nl_linear_ln_small(x.data_ptr(), x.stride(0), gamma.data_ptr(), beta.data_ptr(), 1e-5,
+                                    W.data_ptr(), W.stride(0), out.data_ptr(), out.stride(0), dt, M, N, K, epi,
+                                    None if b is None else b.data_ptr(), None if aux is None else aux.data_ptr(),
+                                    None, _stream())
+        assert st == expect
+        torch.cuda.synchronize()
+
+    C = torch.empty(M, N, device=cuda)
+    run(C, _lib.EPI_STORE)
+    assert ((C - ref).abs().max() / ref.abs().max()).item() < 1e-3
+    U = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    A = torch.empty_like(U)
+    run(U, _lib.EPI_BIAS_GELU, bias, A)
+    pre = ref + bias
+    assert ((A.float() - pre).abs().max() / pre.abs().max()).item() < 1e-2
+    gl = torch.nn.functional.gelu(pre, approximate="tanh")
+    assert ((U.float() - gl).abs().max() / gl.abs().max()).item() < 1e-2
+    assert _lib.device_error() == 0
+
+
+def test_linear_ln_small_declines_large_batch(cuda):
+    x = torch.zeros(9, 512, device=cuda, dtype=torch.bfloat16)
+    W = torch.zeros(512, 512, device=cuda, dtype=torch.bfloat16)
+    g = torch.ones(512, device=cuda)
+    C = torch.empty(9, 512, device=cuda)
+    st = lib.nl_linear_ln_small(x.data_ptr(), 512, g.data_ptr(), g.data_ptr(), 1e-5, W.data_ptr(), 512,
+                                C.data_ptr(), 512, _lib.F32, 9, 512, 512, _lib.EPI_STORE, None, None, None,
+                                _stream())
+    assert st == -1  # NL_ERR_SHAPE: the caller runs LayerNorm + GEMM instead
