@@ -213,13 +213,23 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
       if (!mbar_wait_warp(s_full, j & 1, ab)) { ok = false; break; }
       tc_fence_after();
       float sv[128];  // raw scores; the softmax scale is folded into the exponent FFMA
+      {  // the four 32-column loads of the row in flight together, one wait
+        uint32_t u0[32], u1[32], u2[32], u3[32];
+        tmem_ld32(trow + COL_S, u0);
+        tmem_ld32(trow + COL_S + 32, u1);
+        tmem_ld32(trow + COL_S + 64, u2);
+        tmem_ld32(trow + COL_S + 96, u3);
+        tmem_wait_ld_tied(u0);
+        tmem_tie(u1);
+        tmem_tie(u2);
+        tmem_tie(u3);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t u[32];
-        tmem_ld32(trow + COL_S + c * 32, u);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) sv[c * 32 + e] = __uint_as_float(u[e]);
+        for (int e = 0; e < 32; ++e) {
+          sv[e] = __uint_as_float(u0[e]);
+          sv[32 + e] = __uint_as_float(u1[e]);
+          sv[64 + e] = __uint_as_float(u2[e]);
+          sv[96 + e] = __uint_as_float(u3[e]);
+        }
       }
       tc_fence_before();
       mbar_arrive(s_free);
