@@ -262,13 +262,19 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha < 1.f)) {
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t u[32];
-            tmem_ld32(trow + COL_O + c * 32, u);
-            tmem_wait_ld();
+          {  // both halves of the O row loaded together, one wait
+            uint32_t u0[32], u1[32];
+            tmem_ld32(trow + COL_O, u0);
+            tmem_ld32(trow + COL_O + 32, u1);
+            tmem_wait_ld_tied(u0);
+            tmem_tie(u1);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
-            tmem_st32(trow + COL_O + c * 32, u);
+            for (int e = 0; e < 32; ++e) {
+              u0[e] = __float_as_uint(__uint_as_float(u0[e]) * alpha);
+              u1[e] = __float_as_uint(__uint_as_float(u1[e]) * alpha);
+            }
+            tmem_st32(trow + COL_O, u0);
+            tmem_st32(trow + COL_O + 32, u1);
           }
           tmem_wait_st();
         }
@@ -293,11 +299,14 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
       const float inv = 1.f / l;
       uint32_t ov[32];
       __nv_bfloat16* orow = p.O + bi * p.os.b + q * p.os.s + hi * p.os.h;
+      uint32_t u0[32], u1[32];  // both 32-column halves of the O row in flight, one wait
+      tmem_ld32(trow + COL_O, u0);
+      tmem_ld32(trow + COL_O + 32, u1);
+      tmem_wait_ld_tied(u0);
+      tmem_tie(u1);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        uint32_t u[32];
-        tmem_ld32(trow + COL_O + c * 32, u);
-        tmem_wait_ld();
+        const uint32_t* u = c ? u1 : u0;
 #pragma unroll
         for (int e = 0; e < 16; ++e)
           ov[e] = pack_bf16x2(__uint_as_float(u[2 * e]) * inv, __uint_as_float(u[2 * e + 1]) * inv);
