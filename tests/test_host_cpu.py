@@ -108,3 +108,32 @@ def test_bucket_reducer_two_ranks_gloo():
     n = out[0].numel()
     exp = torch.arange(n, dtype=torch.float32) * 1.5   # mean of x1 and x2
     assert torch.allclose(out[0], exp) and torch.allclose(out[1], exp)
+
+
+def test_lce_chunk_balancing():
+    """The LM-head backward's vocabulary chunks: multiples of 256 columns that
+    cover V in equal parts (no thin tail), at most the target width + 255."""
+    from nlearn_b200.kernels.cross_entropy import _balanced_chunk
+    for V in (50257, 2050, 12000, 100, 1):
+        for target in (64, 4096, 16384, 65536):
+            c = _balanced_chunk(V, target)
+            assert c % 256 == 0 and c >= 256
+            n = -(-V // c)
+            tail = V - (n - 1) * c
+            assert n == 1 or tail > c // 2 or c == 256  # no thin tail chunk
+    assert _balanced_chunk(50257, 16384) == 16896 and _balanced_chunk(50257, 65536) == 50432
+
+
+def test_sampler_restatement_properties():
+    """oracle.decode.sample: deterministic in (seed, pos, row), greedy at
+    temperature 0, and Gumbel-max frequencies follow softmax(logits / T)."""
+    from oracle import decode as OD
+    lg = np.log(np.array([[0.5, 0.3, 0.15, 0.05]], np.float32))
+    assert OD.sample(lg, 1, 2, 0.0)[0] == 0
+    a = [OD.sample(lg, s, 7, 1.0)[0] for s in range(4000)]
+    b = [OD.sample(lg, s, 7, 1.0)[0] for s in range(4000)]
+    assert a == b
+    freq = np.bincount(a, minlength=4) / len(a)
+    assert np.abs(freq - np.array([0.5, 0.3, 0.15, 0.05])).max() < 0.03, freq
+    u = OD.uniforms(3, 5, 0, 1000)
+    assert u.min() > 0 and u.max() < 1 and abs(float(u.mean()) - 0.5) < 0.05
