@@ -4,7 +4,8 @@
 
 CASE is one of: head_fwd, head_bwd (fused LM-head CE), gemm (plain GEMM;
 --layout nn|nt|tn|tt gives the transposition of A and B as in gemm_ex),
-attn_fwd, attn_bwd, ce (materialised-logit CE fwd+bwd, in place).  Prints one
+attn_fwd, attn_bwd, ce (materialised-logit CE fwd+bwd, in place), colsum (bias
+gradient: column sums of a bf16 [M, N]).  Prints one
 JSON line with the CUDA-event time per call and the achieved TFLOP/s or GB/s.
 Small shapes make it the command to run under Nsight Compute for one kernel.
 """
@@ -105,6 +106,14 @@ def main(argv=None):
             ms = _time(lambda: A._flash_bwd_raw(Q, K, V, O, L, dO), a.iters)
             flop = 2.5 * fwd
         out.update(heads=n, seq=s, ms=ms, tflops=flop / ms / 1e9)
+    elif a.case == "colsum":
+        from . import _lib
+        M, N = a.M, a.N
+        x = torch.randn(M, N, device=dev).bfloat16()
+        o = torch.zeros(N, device=dev)
+        ms = _time(lambda: _lib.check(_lib.lib.nl_colsum_bf16(_lib.ptr(x), _lib.ptr(o), M, N, _lib.stream_handle()),
+                                      "colsum"), a.iters)
+        out.update(M=M, N=N, ms=ms, gbs=M * N * 2 / ms / 1e6)
     elif a.case == "ce":
         from .kernels.cross_entropy import ce_fwd_bwd
         M, V = a.M, a.N
