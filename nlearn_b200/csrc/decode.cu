@@ -1,4 +1,6 @@
 // Inference path: one-token decode steps over a KV cache.
+// A device position outside the cache (or past the output row) is reported
+// through the library's device error word (code 3) and nothing is written.
 //
 // Replaces the reference's generate loop (nlearn/model.py:417-465), which runs
 // the whole model on the full token buffer for every new token and samples
@@ -60,6 +62,7 @@ struct AttnParams {
   int* count;                    // [B*H], zero between calls (the merging CTA resets it)
   int B, H, S_max, nsplit;
   float scale_log2;              // log2(e) / sqrt(HD)
+  int* err;                      // device error word
 };
 
 __global__ void __launch_bounds__(kThreads) decode_attn_kernel(AttnParams p) {
@@ -74,6 +77,10 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(AttnParams p) {
   const int D = p.H * HD;
   const int t = *p.pos;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (t < 0 || t >= p.S_max) {  // no cache row for this position: report, touch nothing
+    if (tid == 0 && bh == 0 && split == 0 && p.err) atomicExch(p.err, 3);
+    return;
+  }
   const long long row_pitch = 3LL * D;
   const __nv_bfloat16* newrow = p.qkv_new + b * row_pitch;
   __nv_bfloat16* cb = p.cache + static_cast<long long>(b) * p.S_max * row_pitch;
@@ -198,7 +205,7 @@ __host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
 __global__ void __launch_bounds__(1024) sample_kernel(const float* __restrict__ logits, long long ldl, int V,
                                                      float inv_temp, int greedy, unsigned long long seed,
                                                      const int* __restrict__ pos, int* __restrict__ tok,
-                                                     int* __restrict__ out, long long ldo) {
+                                                     int* __restrict__ out, long long ldo, int* err) {
   griddep_sync();
   __shared__ float bv[32];
   __shared__ int bi[32];
@@ -250,7 +257,10 @@ __global__ void __launch_bounds__(1024) sample_kernel(const float* __restrict__ 
     }
     if (lane == 0) {
       tok[b] = bidx;
-      if (out) out[b * ldo + t + 1] = bidx;
+      if (out) {
+        if (t + 1 >= 0 && t + 1 < ldo) out[b * ldo + t + 1] = bidx;
+        else if (err) atomicExch(err, 3);  // position past the output row: reported, not written
+      }
     }
   }
 }
@@ -302,6 +312,7 @@ extern "C" int nl_decode_attention(const void* qkv_new, void* cache, void* o, co
   p.S_max = S_max;
   p.nsplit = nsplit;
   p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(dec::HD));
+  p.err = device_error_word();
   launch_kernel(dec::decode_attn_kernel, dim3(B * H, nsplit), dim3(dec::kThreads), 0, stream, 1, p);
   return launch_status();
 }
@@ -312,7 +323,7 @@ extern "C" int nl_sample_tokens(const float* logits, long long ldl, int V, float
   if (B <= 0 || V <= 0 || ldl < V || !pos || !tok) return NL_ERR_SHAPE;
   const int greedy = temperature <= 0.f;
   launch_kernel(dec::sample_kernel, dim3(B), dim3(1024), 0, stream, 1, logits, ldl, V,
-                greedy ? 1.f : 1.f / temperature, greedy, seed, pos, tok, out, ldo);
+                greedy ? 1.f : 1.f / temperature, greedy, seed, pos, tok, out, ldo, device_error_word());
   return launch_status();
 }
 

@@ -123,6 +123,8 @@ inline int sm_count() {
 
 // Number of kernels this library has launched (all devices, all threads).
 void count_launch();
+// This device's error word (bounded-wait timeouts, guards), read by nl_get_device_error.
+int* device_error_word();
 
 inline int launch_status() {
   count_launch();

@@ -185,3 +185,33 @@ def test_linear_ln_small_declines_large_batch(cuda):
                                 C.data_ptr(), 512, _lib.F32, 9, 512, 512, _lib.EPI_STORE, None, None, None,
                                 _stream())
     assert st == -1  # NL_ERR_SHAPE: the caller runs LayerNorm + GEMM instead
+
+
+def test_position_guards(cuda):
+    """A device position outside the cache (or past the output row) is
+    reported through the device error word and nothing is written."""
+    B, H, S, D = 1, 8, 256, 512
+    cache = torch.randn(B, S, 3 * D, device=cuda).bfloat16()
+    before = cache.clone()
+    new = torch.randn(B, 3 * D, device=cuda).bfloat16()
+    o = torch.zeros(B, D, device=cuda, dtype=torch.bfloat16)
+    nb = lib.nl_decode_workspace_bytes(B, H, S)
+    ws = torch.zeros(nb, device=cuda, dtype=torch.uint8)
+    assert _lib.device_error() == 0
+    for bad in (S, -1):
+        pos = torch.tensor([bad], device=cuda, dtype=torch.int32)
+        assert lib.nl_decode_attention(new.data_ptr(), cache.data_ptr(), o.data_ptr(), pos.data_ptr(),
+                                       ws.data_ptr(), nb, B, H, S, 64, _stream()) == 0
+        torch.cuda.synchronize()
+        assert _lib.device_error() == 3
+        assert torch.equal(cache, before)
+    logits = torch.randn(B, 64, device=cuda)
+    tok = torch.zeros(B, device=cuda, dtype=torch.int32)
+    out = torch.full((B, 8), -5, device=cuda, dtype=torch.int32)
+    pos = torch.tensor([7], device=cuda, dtype=torch.int32)  # would write out[:, 8] of an 8-wide row
+    assert lib.nl_sample_tokens(logits.data_ptr(), 64, 64, 0.0, 0, pos.data_ptr(), tok.data_ptr(), out.data_ptr(),
+                                8, B, _stream()) == 0
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 3
+    assert (out == -5).all() and tok.item() == int(logits.argmax())
+    assert _lib.device_error() == 0  # reading cleared it
