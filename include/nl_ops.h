@@ -12,8 +12,9 @@
  *  - work is enqueued on `stream`; nothing synchronises, nothing allocates
  *    (scratch, where needed, is a caller-provided workspace);
  *  - the return value is an nl_status: 0 on success, negative on a rejected
- *    shape / alignment / dtype or a failed launch.  Kernel-side timeouts of the
- *    bounded waits are reported through nl_get_device_error().
+ *    shape / alignment / dtype or a failed launch.  Kernel-side conditions
+ *    (bounded-wait timeouts, position guards) are reported through
+ *    nl_get_device_error().
  */
 #ifndef NL_OPS_H
 #define NL_OPS_H
@@ -59,8 +60,9 @@ typedef enum {
 
 /* Library / device introspection. */
 NL_API const char* nl_version(void);
-/* Reads and clears the device-side error word (1 = a bounded wait timed out).
- * Synchronises `stream`. */
+/* Reads and clears the device-side error word (1 = a bounded wait timed out,
+ * 2 = misaligned shared memory, 3 = a decode position outside the KV cache or
+ * the output row).  Synchronises `stream`. */
 NL_API int nl_get_device_error(cudaStream_t stream);
 /* Kernels launched by this library so far in this process (host-side count). */
 NL_API long long nl_launch_count(void);
