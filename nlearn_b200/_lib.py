@@ -120,7 +120,9 @@ def ptr(t) -> c_void_p:
 def device_error() -> int:
     """Read and clear the kernels' device error word: 1 = a bounded wait gave
     up, 2 = misaligned shared memory, 3 = a decode position outside the cache
-    or the output row (nothing written)."""
+    or the output row (the cache and the output row are not written; the
+    attention output keeps its previous contents, the sampled token is still
+    written)."""
     return lib.nl_get_device_error(stream_handle())
 
 

@@ -34,8 +34,10 @@
 //   warps 2-9  one key row per thread, two warps per row quarter splitting the
 //              query columns: P^T = exp2(S^T scale log2e - L log2e),
 //              dS^T = P^T (dP^T - D); P^T -> bf16 in TMEM, dS^T -> bf16 shared memory
-//   warps 10-13 dQ_i tile: TMEM -> float4 atomics into an f32 accumulator
+//   warps 10-13 dQ_i tile: TMEM -> swizzled f32 staging -> TMA bulk reduce-add
+//              into an f32 accumulator
 // followed by a convert kernel dQ = bf16(scale * dQacc).
+#include <atomic>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <math.h>
@@ -921,17 +923,22 @@ static __device__ __align__(256) float g_bwd_scratch[kNoAllocMaxRows * (64 + 1)]
 namespace {
 // Device address of g_bwd_scratch, resolved once per device on that device's
 // first call (host code may not use the symbol itself as a pointer).
+// Host threads may make their first call on a device concurrently: the cache
+// entries are atomics (every thread that resolves the address stores the same
+// value, so a lost race costs one extra cudaGetSymbolAddress, nothing more).
 float* noalloc_scratch() {
   constexpr int kMaxDev = 64;
-  static float* addr[kMaxDev] = {nullptr};
+  static std::atomic<float*> addr[kMaxDev];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return nullptr;
-  if (!addr[dev]) {
+  float* a = addr[dev].load(std::memory_order_acquire);
+  if (!a) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_bwd_scratch) != cudaSuccess) return nullptr;
-    addr[dev] = static_cast<float*>(p);
+    a = static_cast<float*>(p);
+    addr[dev].store(a, std::memory_order_release);
   }
-  return addr[dev];
+  return a;
 }
 }  // namespace
 

@@ -125,8 +125,11 @@ def gemm(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
 
 
 def matmul(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
-    """``A @ B``: plain 2-D x 2-D CUDA matmuls go to the kernel (gemm.py:82-90)."""
-    if A.dim() == 2 and B.dim() == 2 and A.is_cuda:
+    """``A @ B``: 2-D x 2-D products go to the kernel; other ranks stay a plain
+    batched matmul on the device, as reference gemm.py:82-90 routes them.
+    CPU tensors raise (there is no CPU path)."""
+    _require_cuda(A, B)
+    if A.dim() == 2 and B.dim() == 2:
         return gemm(A, B)
     return torch.matmul(A, B)
 
@@ -154,8 +157,10 @@ class _Linear(torch.autograd.Function):
 
 
 def linear(x: torch.Tensor, W: torch.Tensor) -> torch.Tensor:
-    """``x[..., K] @ W[K, N] -> [..., N]`` as one flattened GEMM, output in x.dtype."""
-    if x.dim() >= 2 and W.dim() == 2 and x.is_cuda:
+    """``x[..., K] @ W[K, N] -> [..., N]`` as one flattened GEMM, output in x.dtype.
+    CPU tensors raise (there is no CPU path)."""
+    _require_cuda(x, W)
+    if x.dim() >= 2 and W.dim() == 2:
         lead = x.shape[:-1]
         K = x.shape[-1]
         N = W.shape[1]
@@ -164,7 +169,7 @@ def linear(x: torch.Tensor, W: torch.Tensor) -> torch.Tensor:
             return y.reshape(*lead, N)
         y = gemm(x.reshape(-1, K), W)
         return y.reshape(*lead, N).to(x.dtype)
-    return torch.matmul(x, W)
+    return torch.matmul(x, W)  # other ranks: a plain device matmul, as reference gemm.py:115
 
 
 __all__ = ["gemm", "matmul", "linear", "gemm_ex"]

@@ -1,6 +1,6 @@
 """Single-kernel microbenchmarks of the hot-path operators at chosen shapes.
 
-    python -m nlearn_b200.profile_cases CASE [--M .. --N .. --K ..] [--iters N]
+    python profile_cases.py CASE [--M .. --N .. --K ..] [--iters N]
 
 CASE is one of: head_fwd, head_bwd (fused LM-head CE), gemm (plain GEMM;
 --layout nn|nt|tn|tt gives the transposition of A and B as in gemm_ex),
@@ -13,8 +13,12 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
+import sys
 
 import torch
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 
 def _time(fn, iters):
@@ -50,7 +54,7 @@ def main(argv=None):
     torch.manual_seed(0)
     out = {"case": a.case}
     if a.case in ("head_fwd", "head_bwd"):
-        from .kernels.cross_entropy import lce_bwd_raw, lce_fwd_raw
+        from nlearn_b200.kernels.cross_entropy import lce_bwd_raw, lce_fwd_raw
         M, D, V = a.M, a.K, a.N
         Vp = (V + 63) // 64 * 64
         X = torch.randn(M, D, device=dev).bfloat16()
@@ -70,7 +74,7 @@ def main(argv=None):
             flop = 4 * M * D * V  # algorithmic: dX + dW (recompute not counted)
         out.update(M=M, D=D, V=V, ms=ms, tflops=flop / ms / 1e9)
     elif a.case == "gemm":
-        from .kernels.gemm import gemm_ex
+        from nlearn_b200.kernels.gemm import gemm_ex
         M, N, K = a.M, a.N, a.K
         at, bt = a.layout[0] == "t", a.layout[1] == "t"
         def mk(r, c):  # rows x cols with row pitch c + pad
@@ -78,11 +82,11 @@ def main(argv=None):
         A = mk(*((K, M) if at else (M, K)))
         B = mk(*((N, K) if bt else (K, N)))
         if a.accum:
-            from .kernels.gemm import EPI_ACCUM
+            from nlearn_b200.kernels.gemm import EPI_ACCUM
             C = torch.zeros(M, N, device=dev, dtype=torch.float32)
             ms = _time(lambda: gemm_ex(A, B, a_trans=at, b_trans=bt, out=C, epilogue=EPI_ACCUM), a.iters)
         else:
-            from . import _lib as L
+            from nlearn_b200 import _lib as L
             C = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
             epi = {"store": L.EPI_STORE, "bias": L.EPI_BIAS, "bias_gelu": L.EPI_BIAS_GELU, "resid": L.EPI_RESID,
                    "dgelu": L.EPI_DGELU}[a.epi]
@@ -94,7 +98,7 @@ def main(argv=None):
         out.update(M=M, N=N, K=K, layout=a.layout, pad=a.pad, accum=a.accum, epi=a.epi, ms=ms,
                    tflops=2 * M * N * K / ms / 1e9)
     elif a.case in ("attn_fwd", "attn_bwd"):
-        from . import attention as A
+        from nlearn_b200 import attention as A
         n, s = a.heads, a.seq
         Q, K, V, dO = (torch.randn(n, s, 64, device=dev).bfloat16() for _ in range(4))
         O, L = A._flash_fwd_raw(Q, K, V)
@@ -107,7 +111,7 @@ def main(argv=None):
             flop = 2.5 * fwd
         out.update(heads=n, seq=s, ms=ms, tflops=flop / ms / 1e9)
     elif a.case == "colsum":
-        from . import _lib
+        from nlearn_b200 import _lib
         M, N = a.M, a.N
         x = torch.randn(M, N, device=dev).bfloat16()
         o = torch.zeros(N, device=dev)
@@ -115,7 +119,7 @@ def main(argv=None):
                                       "colsum"), a.iters)
         out.update(M=M, N=N, ms=ms, gbs=M * N * 2 / ms / 1e6)
     elif a.case == "ce":
-        from .kernels.cross_entropy import ce_fwd_bwd
+        from nlearn_b200.kernels.cross_entropy import ce_fwd_bwd
         M, V = a.M, a.N
         x = torch.randn(M, V, device=dev)
         t = torch.randint(0, V, (M,), device=dev, dtype=torch.int32)

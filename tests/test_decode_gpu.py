@@ -189,12 +189,13 @@ def test_linear_ln_small_declines_large_batch(cuda):
 
 def test_position_guards(cuda):
     """A device position outside the cache (or past the output row) is
-    reported through the device error word and nothing is written."""
+    reported through the device error word; the cache, the attention output
+    and the output row are left untouched (the sampled token is written)."""
     B, H, S, D = 1, 8, 256, 512
     cache = torch.randn(B, S, 3 * D, device=cuda).bfloat16()
     before = cache.clone()
     new = torch.randn(B, 3 * D, device=cuda).bfloat16()
-    o = torch.zeros(B, D, device=cuda, dtype=torch.bfloat16)
+    o = torch.full((B, D), 0.5, device=cuda, dtype=torch.bfloat16)
     nb = lib.nl_decode_workspace_bytes(B, H, S)
     ws = torch.zeros(nb, device=cuda, dtype=torch.uint8)
     assert _lib.device_error() == 0
@@ -205,6 +206,7 @@ def test_position_guards(cuda):
         torch.cuda.synchronize()
         assert _lib.device_error() == 3
         assert torch.equal(cache, before)
+        assert (o == 0.5).all()       # not recomputed: stale contents stay
     logits = torch.randn(B, 64, device=cuda)
     tok = torch.zeros(B, device=cuda, dtype=torch.int32)
     out = torch.full((B, 8), -5, device=cuda, dtype=torch.int32)

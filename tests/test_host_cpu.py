@@ -137,3 +137,19 @@ def test_sampler_restatement_properties():
     assert np.abs(freq - np.array([0.5, 0.3, 0.15, 0.05])).max() < 0.03, freq
     u = OD.uniforms(3, 5, 0, 1000)
     assert u.min() > 0 and u.max() < 1 and abs(float(u.mean()) - 0.5) < 0.05
+
+
+def test_operators_refuse_cpu_tensors():
+    """The operator surface has no CPU path: CPU tensors raise before any
+    library call (no silent fallback to torch.matmul)."""
+    from nlearn_b200.kernels.gemm import linear, matmul, gemm_ex
+    from nlearn_b200.kernels.cross_entropy import cross_entropy, linear_cross_entropy
+    from nlearn_b200.attention import attention
+    x = torch.randn(4, 8, 16)
+    W = torch.randn(16, 8)
+    for fn, args in ((linear, (x, W)), (matmul, (x[0], W)), (gemm_ex, (x[0].bfloat16(), W.bfloat16())),
+                     (cross_entropy, (torch.randn(4, 10), torch.zeros(4, dtype=torch.long))),
+                     (linear_cross_entropy, (x[0], W, torch.zeros(8, dtype=torch.long))),
+                     (attention, (torch.randn(2, 8, 64),) * 3)):
+        with pytest.raises(ValueError):
+            fn(*args)

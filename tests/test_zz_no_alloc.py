@@ -6,8 +6,11 @@ buffers, or code running where cudaMalloc is not allowed.  This entry point
 takes no workspace: its scratch is a fixed array inside the library.  The test
 calls it through the C ABI twice in a row (the shared scratch keeps the first
 call's contents, so the second call checks that it is cleared) and compares
-with the workspace-taking nl_flash_attention_bwd at the attention tests'
-tolerance (max |err| / max |ref| <= 1e-2).  This file is collected last, and
+with the workspace-taking nl_flash_attention_bwd: dK and dV come from the same
+kernels and accumulation order and must be bit-identical; dQ is summed by
+reduce-adds whose order can vary, so it is held to the attention tests'
+tolerance (max |err| / max |ref| <= 1e-2).  One case fills the array to its
+last row, so a misplaced D vector would be caught there.  This file is collected last, and
 also passes on its own in a fresh process."""
 import pytest
 import torch
@@ -32,7 +35,7 @@ def _noalloc(Q, K, V, O, dO, L):
     return dQ, dK, dV
 
 
-@pytest.mark.parametrize("n,s", [(32, 512), (6, 300)])
+@pytest.mark.parametrize("n,s", [(32, 512), (6, 300), (256, 512)])
 def test_noalloc_matches_workspace_entry(cuda, n, s):
     torch.manual_seed(n + s)
     Q, K, V, dO = (torch.randn(n, s, 64, device=cuda).bfloat16() for _ in range(4))
@@ -41,8 +44,8 @@ def test_noalloc_matches_workspace_entry(cuda, n, s):
     for _ in range(2):                               # two calls in a row share the scratch
         got = _noalloc(Q, K, V, O, dO, L)
         torch.cuda.synchronize()
-        for g, r in zip(got, ref):
-            assert nrel(g, r) < TOL
+        assert nrel(got[0], ref[0]) < TOL
+        assert torch.equal(got[1], ref[1]) and torch.equal(got[2], ref[2])
     assert lib.nl_get_device_error(stream_handle()) == 0
 
 
