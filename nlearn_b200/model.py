@@ -17,7 +17,15 @@ Per block (M = batch*seq rows, activations bf16):
     h2  = LN2(x2)
     u   = gelu(h2 @ W1 + b1)  (pre-act saved)      nl_gemm_ex (bias+GELU epilogue)
     x3  = x2 + u @ W2 + b2                         nl_gemm_ex (bias+residual epilogue)
-then LN_f and the fused LM-head CE (nl_lce_fwd / nl_lce_bwd).  The backward
+then LN_f and the loss, on one of the reference's two paths
+(nlearn/train.py:270-285, chosen by NLEARN_FUSED_LMHEAD):
+    fused (NLEARN_FUSED_LMHEAD=1, and the default here when the variable is
+    unset): the LM-head CE without logits, nl_lce_fwd / nl_lce_bwd;
+    materialised (NLEARN_FUSED_LMHEAD=0; the reference's default): logits =
+    linear(h_f, W_head) as bf16 [M, V] (nl_gemm_ex), then the `ce_fwd` /
+    `ce_bwd` pair as one fused pass writing dlogits over the logits in place
+    (nl_ce_fwd_bwd), then dX = dlogits W^T and dW += h_f^T dlogits.
+The backward
 mirrors it; every weight gradient GEMM accumulates (f32) straight into its
 slot of one flat gradient buffer, which the data-parallel reducer all-reduces
 in buckets and AdamW consumes in place.
@@ -25,6 +33,7 @@ in buckets and AdamW consumes in place.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -32,7 +41,14 @@ import torch
 from . import _lib
 from ._lib import check, lib, ptr, stream_handle
 from .kernels.gemm import gemm_ex
-from .kernels.cross_entropy import lce_bwd_raw, lce_fwd_raw
+from .kernels.cross_entropy import ce_fwd_bwd, lce_bwd_raw, lce_fwd_raw
+
+
+def fused_lmhead_default() -> bool:
+    """NLEARN_FUSED_LMHEAD as nlearn/train.py:28 reads it ("1" selects the
+    fused LM-head CE), except that unset also means fused here: on B200 the
+    fused path is the default and "0" selects the materialised one."""
+    return os.environ.get("NLEARN_FUSED_LMHEAD", "1") != "0"
 
 
 @dataclass(frozen=True)
@@ -148,9 +164,10 @@ def _ln_bwd(dy, x, mean, rstd, g, dres, dres_bf, dg, db, M, D, accumulate):
 class GPT:
     """Forward + backward of the BASELINE GPT on one device's micro-batch."""
 
-    def __init__(self, cfg: GPTConfig, params: FlatParams):
+    def __init__(self, cfg: GPTConfig, params: FlatParams, fused_lmhead: bool | None = None):
         self.cfg = cfg
         self.P = params
+        self.fused_lmhead = fused_lmhead_default() if fused_lmhead is None else bool(fused_lmhead)
 
     # ------------------------------------------------------------------ forward
     def forward(self, tok: torch.Tensor, targets: torch.Tensor):
@@ -187,12 +204,21 @@ class GPT:
         hf, mf, rf = _ln_fwd(x, P.f("lnf.g"), P.f("lnf.b"), cfg.ln_eps, M, D)
         t = targets.reshape(-1)
         V = cfg.vocab
-        loss_rows, lse = lce_fwd_raw(hf, P.p("head.w")[:, :V], t)
-        saved.update(xf=x, hf=hf, mf=mf, rf=rf, lse=lse)
+        saved.update(xf=x, hf=hf, mf=mf, rf=rf)
+        if self.fused_lmhead:
+            loss_rows, lse = lce_fwd_raw(hf, P.p("head.w")[:, :V], t)
+            saved["lse"] = lse
+        else:
+            # logits bf16 [M, V] at the head's padded row pitch, then loss, lse and
+            # dlogits = (softmax - onehot) / M from one read, written in place
+            logits = torch.empty(M, cfg.vocab_padded, device=dev, dtype=torch.bfloat16)[:, :V]
+            gemm_ex(hf, P.p("head.w")[:, :V], out=logits)
+            loss_rows, lse, _ = ce_fwd_bwd(logits, t, out=logits)
+            saved.update(lse=lse, dlogits=logits)
         return loss_rows.mean(), saved
 
     # ------------------------------------------------------------------ backward
-    def backward(self, saved, grad_scale: torch.Tensor | None = None, on_grad_ready=None):
+    def backward(self, saved, on_grad_ready=None):
         """Accumulates d(mean loss) into P.grad.  ``on_grad_ready(name)`` is
         called once a parameter's gradient is final AND the backward has made
         its last read of that parameter, so the callee may reduce the gradient
@@ -203,12 +229,18 @@ class GPT:
         dev = saved["hf"].device
         notify = on_grad_ready or (lambda name: None)
         t = saved["targets"].reshape(-1)
-        # LM head + CE: dhf (f32) and d head.w accumulated in place
-        dhf = torch.zeros(M, D, device=dev, dtype=torch.float32)
-        lce_bwd_raw(saved["hf"], P.p("head.w")[:, :V], t, saved["lse"], g=grad_scale, dX=dhf,
-                    dW=P.g("head.w")[:, :V], dw_accumulate=True)
-        notify("head.w")
-        dhf_bf = dhf.to(torch.bfloat16)
+        if self.fused_lmhead:
+            # LM head + CE: dhf (f32) and d head.w accumulated in place
+            dhf = torch.zeros(M, D, device=dev, dtype=torch.float32)
+            lce_bwd_raw(saved["hf"], P.p("head.w")[:, :V], t, saved["lse"], dX=dhf,
+                        dW=P.g("head.w")[:, :V], dw_accumulate=True)
+            notify("head.w")
+            dhf_bf = dhf.to(torch.bfloat16)
+        else:
+            dl = saved["dlogits"]                      # bf16 [M, V], already / M
+            gemm_ex(saved["hf"], dl, a_trans=True, out=P.g("head.w")[:, :V], epilogue=_lib.EPI_ACCUM)
+            dhf_bf = gemm_ex(dl, P.p("head.w")[:, :V], b_trans=True, out_dtype=torch.bfloat16)
+            notify("head.w")
         dres = torch.empty(M, D, device=dev, dtype=torch.float32)
         dres_bf = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
         _ln_bwd(dhf_bf, saved["xf"], saved["mf"], saved["rf"], P.f("lnf.g"), dres, dres_bf, P.g("lnf.g"),

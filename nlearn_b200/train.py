@@ -147,6 +147,7 @@ class TrainConfig:
     weight_decay: float = 0.1
     seed: int = 0
     bucket_mb: int = 64
+    fused_lmhead: bool | None = None   # None: NLEARN_FUSED_LMHEAD (model.fused_lmhead_default)
 
 
 class Trainer:
@@ -155,7 +156,7 @@ class Trainer:
         self.device = torch.device(device)
         self.rank, self.world = rank, world
         self.P = FlatParams(cfg, self.device, seed=tcfg.seed)   # same init on every rank
-        self.model = GPT(cfg, self.P)
+        self.model = GPT(cfg, self.P, fused_lmhead=tcfg.fused_lmhead)
         self.opt = AdamW(self.P, weight_decay=tcfg.weight_decay)
         # with more than one rank the optimizer runs per bucket, overlapped with
         # the remaining backward, right after that bucket's all-reduce

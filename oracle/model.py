@@ -13,6 +13,14 @@ and optimizer the headline metric trains:
 Parity of the optimizer is unpinned by any reference test (optax is a
 third-party dependency absent here); the formulas are restated.
 
+Pinned: tests/golden/ln_gelu.npz (the reference's ln_gelu) pins
+``layer_norm`` + ``gelu_tanh`` + residual; the flash fixtures' ``O_std``
+(the reference's ``_attention_standard``) pin ``causal_attention``; and
+tests/golden/model_small.npz pins ``OracleGPT.hidden`` / ``logits`` / ``loss``
+on a small model run through the reference's own ``block_forward``,
+``linear``, ``attention`` and one-hot ``cross_entropy``.  The gradients are
+autograd of that pinned forward.
+
 Parameters are keyed by the same names as nlearn_b200.model.param_specs so
 tests can load the exact initial weights of the GPU run.  Only tests/,
 __graft_entry__.smoke() and bench.py's CPU-baseline leg use this module.
@@ -25,38 +33,60 @@ import torch
 import torch.nn.functional as F
 
 
+def layer_norm(x, g, b, eps=1e-5):
+    """LayerNorm with gain and bias over the last dim, biased variance
+    (iree_metal/kernels/test/bf16_metal_test.py:8-10)."""
+    return F.layer_norm(x, (x.shape[-1],), g, b, eps)
+
+
+def gelu_tanh(h):
+    """tanh-approximated GELU (bf16_metal_test.py:11)."""
+    return F.gelu(h, approximate="tanh")
+
+
+def causal_attention(Q, K, V):
+    """softmax(Q K^T / sqrt(d) + causal mask) V over [..., s, d]
+    (nlearn/attention.py:138-156 `_attention_standard`)."""
+    S = Q.shape[-2]
+    mask = torch.triu(torch.ones(S, S, dtype=torch.bool), 1)
+    sc = (Q @ K.transpose(-1, -2)) / math.sqrt(Q.shape[-1])
+    return torch.softmax(sc.masked_fill(mask, float("-inf")), -1) @ V
+
+
 class OracleGPT:
     def __init__(self, params: dict, n_layers=4, n_heads=8, vocab=50257, eps=1e-5):
         # params: name -> f32 CPU tensor (head.w may be column-padded)
-        self.p = {k: v.detach().clone().float().requires_grad_(True) for k, v in params.items()}
+        self.p = {k: torch.as_tensor(v).detach().clone().float().requires_grad_(True) for k, v in params.items()}
         self.L, self.H, self.V, self.eps = n_layers, n_heads, vocab, eps
 
     def loss(self, tok: torch.Tensor, tgt: torch.Tensor) -> torch.Tensor:
         logits = self.logits(tok)
         return F.cross_entropy(logits.reshape(-1, self.V), tgt.reshape(-1).long())
 
-    def logits(self, tok: torch.Tensor) -> torch.Tensor:
-        """[B, S] tokens -> [B, S, V] f32 logits (the model forward of
-        nlearn/model.py:361-398 at the BASELINE architecture)."""
+    def hidden(self, tok: torch.Tensor) -> torch.Tensor:
+        """[B, S] tokens -> final-LayerNorm hidden states [B, S, D]: the
+        pre-LN block wiring of nlearn/model.py:315-324 (x += attn(LN1 x);
+        x += ffn(LN2 x)) at the BASELINE architecture."""
         p, H = self.p, self.H
         B, S = tok.shape
         D = p["wte"].shape[1]
         x = p["wte"][tok.long()] + p["wpe"][:S][None]
-        mask = torch.triu(torch.ones(S, S, dtype=torch.bool), 1)
         for layer in range(self.L):
             q = f"blocks.{layer}."
-            h = F.layer_norm(x, (D,), p[q + "ln1.g"], p[q + "ln1.b"], self.eps)
+            h = layer_norm(x, p[q + "ln1.g"], p[q + "ln1.b"], self.eps)
             qkv = (h @ p[q + "wqkv"]).view(B, S, 3, H, D // H)
             Q, K, V = (qkv[:, :, i].transpose(1, 2) for i in range(3))
-            sc = (Q @ K.transpose(-1, -2)) / math.sqrt(D // H)
-            sc = sc.masked_fill(mask, float("-inf"))
-            o = (torch.softmax(sc, -1) @ V).transpose(1, 2).reshape(B, S, D)
+            o = causal_attention(Q, K, V).transpose(1, 2).reshape(B, S, D)
             x = x + o @ p[q + "wo"]
-            h = F.layer_norm(x, (D,), p[q + "ln2.g"], p[q + "ln2.b"], self.eps)
-            u = F.gelu(h @ p[q + "w1"] + p[q + "b1"], approximate="tanh")
+            h = layer_norm(x, p[q + "ln2.g"], p[q + "ln2.b"], self.eps)
+            u = gelu_tanh(h @ p[q + "w1"] + p[q + "b1"])
             x = x + u @ p[q + "w2"] + p[q + "b2"]
-        h = F.layer_norm(x, (D,), p["lnf.g"], p["lnf.b"], self.eps)
-        return h @ p["head.w"][:, :self.V]
+        return layer_norm(x, p["lnf.g"], p["lnf.b"], self.eps)
+
+    def logits(self, tok: torch.Tensor) -> torch.Tensor:
+        """[B, S] tokens -> [B, S, V] f32 logits (the model forward of
+        nlearn/model.py:361-398 at the BASELINE architecture)."""
+        return self.hidden(tok) @ self.p["head.w"][:, :self.V]
 
     def grads(self):
         return {k: (v.grad if v.grad is not None else torch.zeros_like(v)) for k, v in self.p.items()}

@@ -73,9 +73,19 @@ def _install_numpy_jax():
     jax.devices = lambda: [_Dev()]
     jax.dtypes = types.SimpleNamespace(float0=np.bool_)
     jax.ffi = types.SimpleNamespace(ffi_call=None)
+    jax.lax = types.SimpleNamespace(rsqrt=lambda v: (1.0 / np.sqrt(v)).astype(np.asarray(v).dtype))
+    jax.jit = lambda f=None, **kw: f if f is not None else (lambda g: g)
+    jax.checkpoint = lambda f, **kw: f
+    jax.tree_util = types.SimpleNamespace(tree_map=lambda fn, t: t)
+    jax.random = types.SimpleNamespace()
+    import ml_dtypes
+    jnp.bfloat16 = ml_dtypes.bfloat16
+    jnp.float16 = np.float16
+    jnp.float32 = np.float32
     jax.ShapeDtypeStruct = None
     sys.modules["jax"] = jax
     sys.modules["jax.numpy"] = jnp
+    sys.modules["jax.random"] = jax.random
 
 
 def _load(ref: Path, rel: str, name: str):
@@ -108,6 +118,86 @@ def _run_test_script(path: Path, drop_from: str | None = None) -> dict:
     g: dict = {"__name__": "golden", "__file__": str(path)}
     exec(compile(ast.Module(body=keep, type_ignores=[]), str(path), "exec"), g)
     return g
+
+
+# Small BASELINE-architecture model for the step fixture (parameters regenerate
+# from the seed; tests/test_oracle_golden.py rebuilds them with this function).
+SMALL = dict(vocab=1000, d_model=128, n_heads=2, n_layers=2, d_ff=512, seq=64, batch=2, seed=11)
+
+
+def small_model_params(cfg=SMALL) -> dict:
+    """Flat-name f32 parameters (nlearn_b200.model.param_specs names) of the
+    small model, from numpy's PCG64 stream (stable across numpy versions)."""
+    rng = np.random.default_rng(cfg["seed"])
+    D, F, V, S = cfg["d_model"], cfg["d_ff"], cfg["vocab"], cfg["seq"]
+    p = {"wte": rng.standard_normal((V, D)) * 0.02, "wpe": rng.standard_normal((S, D)) * 0.02,
+         "head.w": rng.standard_normal((D, V)) * 0.02,
+         "lnf.g": 1 + 0.1 * rng.standard_normal(D), "lnf.b": 0.1 * rng.standard_normal(D)}
+    for i in range(cfg["n_layers"]):
+        q = f"blocks.{i}."
+        p.update({q + "ln1.g": 1 + 0.1 * rng.standard_normal(D), q + "ln1.b": 0.1 * rng.standard_normal(D),
+                  q + "wqkv": rng.standard_normal((D, 3 * D)) * 0.05, q + "wo": rng.standard_normal((D, D)) * 0.05,
+                  q + "ln2.g": 1 + 0.1 * rng.standard_normal(D), q + "ln2.b": 0.1 * rng.standard_normal(D),
+                  q + "w1": rng.standard_normal((D, F)) * 0.05, q + "b1": 0.1 * rng.standard_normal(F),
+                  q + "w2": rng.standard_normal((F, D)) * 0.05, q + "b2": 0.1 * rng.standard_normal(D)})
+    tok = rng.integers(0, V, (cfg["batch"], S + 1))
+    return {k: np.asarray(v, np.float32) for k, v in p.items()}, tok[:, :-1].astype(np.int32), \
+        tok[:, 1:].astype(np.int32)
+
+
+def small_model_fixture(ref: Path, attn, ce) -> dict:
+    gemm_mod = _load(ref, "nlearn/kernels/gemm.py", "nlearn.kernels.gemm")
+    pkg = types.ModuleType("nlearn")
+    kpkg = types.ModuleType("nlearn.kernels")
+    pkg.attention, pkg.kernels, kpkg.gemm = attn, kpkg, gemm_mod
+    sys.modules.update({"nlearn": pkg, "nlearn.attention": attn, "nlearn.kernels": kpkg,
+                        "nlearn.kernels.gemm": gemm_mod})
+    model = _load(ref, "nlearn/model.py", "nlearn.model")
+    cfg = SMALL
+    H, D = cfg["n_heads"], cfg["d_model"]
+    linear = model.linear                       # reference linear (jnp.matmul off IREE-Metal)
+    assert not gemm_mod.USE_IREE_GEMM and not attn.USE_IREE_FLASH and not attn.HAS_CUDNN
+
+    def layer_norm(p, x):                       # the LayerNorm of ln_gelu (bf16_metal_test.py:8-10)
+        mu = x.mean(-1, keepdims=True)
+        var = ((x - mu) ** 2).mean(-1, keepdims=True)
+        return (x - mu) * (1.0 / np.sqrt(var + 1e-5)) * p["gamma"] + p["beta"]
+
+    def gelu(h):                                # the GELU of ln_gelu (bf16_metal_test.py:11)
+        return 0.5 * h * (1 + np.tanh(0.7978845608 * (h + 0.044715 * h ** 3)))
+
+    def attention_forward(p, x):                # model.py:159-198 without QK-norm / RoPE
+        bs, s, _ = x.shape
+
+        def proj(W):
+            return linear(x, W).reshape(bs, s, H, D // H).transpose(0, 2, 1, 3).reshape(bs * H, s, D // H)
+        o = model.attention(proj(p["W_q"]), proj(p["W_k"]), proj(p["W_v"]))
+        o = o.reshape(bs, H, s, D // H).transpose(0, 2, 1, 3).reshape(bs, s, D)
+        return linear(o, p["W_o"])
+
+    def ffn_forward(p, x):                      # GELU FFN with biases (the BASELINE FFN)
+        return linear(gelu(linear(x, p["W_up"]) + p["b_up"]), p["W_down"]) + p["b_down"]
+
+    model.layer_norm, model.attention_forward, model.ffn_forward = layer_norm, attention_forward, ffn_forward
+    named, tok, tgt = small_model_params(cfg)
+    blocks = []
+    for i in range(cfg["n_layers"]):
+        q = f"blocks.{i}."
+        w = named[q + "wqkv"]
+        blocks.append({"ln1": {"gamma": named[q + "ln1.g"], "beta": named[q + "ln1.b"]},
+                       "attn": {"W_q": w[:, :D], "W_k": w[:, D:2 * D], "W_v": w[:, 2 * D:], "W_o": named[q + "wo"]},
+                       "ln2": {"gamma": named[q + "ln2.g"], "beta": named[q + "ln2.b"]},
+                       "ffn": {"W_up": named[q + "w1"], "b_up": named[q + "b1"], "W_down": named[q + "w2"],
+                               "b_down": named[q + "b2"]}})
+    x = named["wte"][tok] + named["wpe"][None, :tok.shape[1]]
+    for bp in blocks:
+        x = model.block_forward(bp, x)          # reference wiring, model.py:315-324
+    h = layer_norm({"gamma": named["lnf.g"], "beta": named["lnf.b"]}, x)
+    logits = linear(h, named["head.w"])
+    loss = ce.cross_entropy(logits, tgt)        # reference one-hot CE fallback
+    lse = np.log(np.exp(logits - logits.max(-1, keepdims=True)).sum(-1)) + logits.max(-1)
+    return dict(hidden=np.asarray(h, np.float32), logits_head=np.asarray(logits[..., :64], np.float32),
+                lse=np.asarray(lse, np.float32), loss=np.float32(loss))
 
 
 def main(ref: Path) -> None:
@@ -169,6 +259,16 @@ def main(ref: Path) -> None:
         Ab = A.astype(ml_dtypes.bfloat16).astype(np.float32)
         Bb = B.astype(ml_dtypes.bfloat16).astype(np.float32)
         out[f"gemm_{label}"] = dict(A=A, B=B, C=(Ab @ Bb).astype(np.float32))
+
+    # 6. training-step pieces: ln_gelu and a small BASELINE model through the
+    #    reference's block_forward / linear / attention / cross_entropy
+    g = _run_test_script(tdir / "bf16_metal_test.py", drop_from="for dt in")
+    rng = np.random.default_rng(6)
+    x = (rng.standard_normal((2, 32, 512)) * 1.5 + 0.3).astype(np.float32)
+    gam = (1.0 + 0.1 * rng.standard_normal(512)).astype(np.float32)
+    bet = (0.1 * rng.standard_normal(512)).astype(np.float32)
+    out["ln_gelu"] = dict(x=x, g=gam, b=bet, y=np.asarray(g["ln_gelu"](x, gam, bet), np.float32))
+    out["model_small"] = small_model_fixture(ref, attn, ce)
 
     for key, rec in out.items():
         np.savez_compressed(HERE / f"{key}.npz", **{k: np.asarray(v) for k, v in rec.items()})

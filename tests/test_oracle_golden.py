@@ -86,3 +86,50 @@ def test_bf16_round_matches_ml_dtypes():
     x = np.random.default_rng(3).standard_normal(10000).astype(np.float32) * 100
     import ml_dtypes
     np.testing.assert_array_equal(ops.bf16_round(x), x.astype(ml_dtypes.bfloat16).astype(np.float32))
+
+
+# ------------------------------------------------------------------ step oracle
+def test_ln_gelu_matches_reference():
+    """oracle.model's LayerNorm + tanh-GELU + residual against the reference's
+    ln_gelu (iree_metal/kernels/test/bf16_metal_test.py:6-12)."""
+    import torch
+    from oracle.model import gelu_tanh, layer_norm
+    g = load("ln_gelu")
+    x = torch.from_numpy(g["x"])
+    y = x + gelu_tanh(layer_norm(x, torch.from_numpy(g["g"]), torch.from_numpy(g["b"])))
+    np.testing.assert_allclose(y.numpy(), g["y"], atol=2e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("name", ["flash_fwd_small", "flash_fwd_tiled"])
+def test_model_attention_matches_reference(name):
+    """The attention inside oracle.model against _attention_standard."""
+    import torch
+    from oracle.model import causal_attention
+    g = load(name)
+    O = causal_attention(*(torch.from_numpy(g[k]) for k in ("Q", "K", "V")))
+    np.testing.assert_allclose(O.numpy(), g["O_std"], atol=1e-5)
+
+
+def test_model_forward_matches_reference_block_wiring():
+    """OracleGPT (hidden states, logits, loss) against a small BASELINE model
+    run through the reference's block_forward / linear / attention /
+    cross_entropy (tests/golden/make_golden.py, section 6)."""
+    import importlib.util
+    import torch
+    from oracle.model import OracleGPT
+    spec = importlib.util.spec_from_file_location("make_golden", G / "make_golden.py")
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    g = load("model_small")
+    named, tok, tgt = mg.small_model_params()
+    cfg = mg.SMALL
+    orc = OracleGPT({k: torch.from_numpy(v) for k, v in named.items()}, n_layers=cfg["n_layers"],
+                    n_heads=cfg["n_heads"], vocab=cfg["vocab"])
+    with torch.no_grad():
+        h = orc.hidden(torch.from_numpy(tok))
+        lg = orc.logits(torch.from_numpy(tok))
+        loss = orc.loss(torch.from_numpy(tok), torch.from_numpy(tgt))
+    np.testing.assert_allclose(h.numpy(), g["hidden"], atol=1e-4, rtol=1e-4)
+    np.testing.assert_allclose(lg[..., :64].numpy(), g["logits_head"], atol=1e-5)
+    np.testing.assert_allclose(torch.logsumexp(lg, -1).numpy(), g["lse"], atol=1e-5)
+    assert abs(float(loss) - float(g["loss"])) < 1e-5
