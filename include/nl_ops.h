@@ -136,6 +136,29 @@ NL_API int nl_flash_attention_bwd_dkdv(const void* Q, const void* K, const void*
                                        const float* L, const float* D, void* dK, void* dV, int n, int s, int d,
                                        cudaStream_t stream);
 
+/* Dtype-dispatching forms of the three targets above, taking operands and
+ * results in the dtype the reference's custom calls carry them: nlearn's
+ * wrappers cast Q, K, V, dO to f32 and receive f32 O, dQ, dK, dV
+ * (nlearn/attention.py:82-91, 97, 111-128; the ABI table of
+ * iree_metal/patches/08-gemm-dispatch-pass.patch:57-123).  `dtype` (NL_F32 or
+ * NL_BF16) applies to Q, K, V, O, dO, dQ, dK, dV; L and D are f32 [n, s].
+ * For NL_F32 the library converts to bf16 tensor-core operands and back on
+ * `stream` inside `workspace` (caller-owned, 256-byte aligned, at least
+ * nl_flash_attention_workspace_bytes(target, n, s, d, dtype) bytes; target
+ * 0 = fwd, 1 = bwd_dq, 2 = bwd_dkdv); dQ is widened from the f32 accumulator.
+ * An XLA FFI handler registered under each reference target name calls these
+ * with the operand order of the table (the handler's scratch allocator
+ * provides the workspace). */
+NL_API size_t nl_flash_attention_workspace_bytes(int target, int n, int s, int d, int dtype);
+NL_API int nl_flash_attention_fwd_dt(const void* Q, const void* K, const void* V, void* O, float* L, int n, int s,
+                                     int d, int dtype, void* workspace, size_t ws_bytes, cudaStream_t stream);
+NL_API int nl_flash_attention_bwd_dq_dt(const void* Q, const void* K, const void* V, const void* dO, const float* L,
+                                        const float* D, void* dQ, int n, int s, int d, int dtype, void* workspace,
+                                        size_t ws_bytes, cudaStream_t stream);
+NL_API int nl_flash_attention_bwd_dkdv_dt(const void* Q, const void* K, const void* V, const void* dO,
+                                          const float* L, const float* D, void* dK, void* dV, int n, int s, int d,
+                                          int dtype, void* workspace, size_t ws_bytes, cudaStream_t stream);
+
 /* Allocation-free variant of nl_flash_attention_bwd, for callers that cannot
  * allocate device memory (no workspace argument).  No counterpart in the
  * reference.  Its scratch (dQ accumulator and D) is a fixed array inside the

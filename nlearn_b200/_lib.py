@@ -39,6 +39,11 @@ SIGNATURES: dict[str, list] = {
     "nl_flash_attention_bwd": [c_void_p] * 11 + [c_int, c_int, c_int, c_void_p],
     "nl_flash_attention_bwd_dq": [c_void_p] * 8 + [c_int, c_int, c_int, c_void_p],
     "nl_flash_attention_bwd_dkdv": [c_void_p] * 8 + [c_int, c_int, c_int, c_void_p],
+    "nl_flash_attention_workspace_bytes": [c_int, c_int, c_int, c_int, c_int],
+    "nl_flash_attention_fwd_dt": [c_void_p] * 5 + [c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p],
+    "nl_flash_attention_bwd_dq_dt": [c_void_p] * 7 + [c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p],
+    "nl_flash_attention_bwd_dkdv_dt": [c_void_p] * 8 + [c_int, c_int, c_int, c_int, c_void_p, c_size_t,
+                                                        c_void_p],
     "nl_flash_attention_bwd_noalloc_max_rows": [],
     "nl_flash_attention_bwd_noalloc": [c_void_p] * 9 + [c_int, c_int, c_int, c_void_p],
     "nl_flash_attention_fwd_strided": [c_void_p] * 3 + [c_longlong] * 3 + [c_void_p] + [c_longlong] * 3 +
@@ -69,7 +74,7 @@ SIGNATURES: dict[str, list] = {
                    c_int, c_int, c_void_p, ctypes.c_size_t, c_int, c_int, c_int, c_int, c_void_p],
 }
 _RESTYPE = {"nl_version": ctypes.c_char_p, "nl_launch_count": c_longlong,
-            "nl_flash_attention_bwd_noalloc_max_rows": c_longlong, "nl_lce_workspace_bytes": ctypes.c_size_t,
+            "nl_flash_attention_bwd_noalloc_max_rows": c_longlong, "nl_flash_attention_workspace_bytes": c_size_t, "nl_lce_workspace_bytes": ctypes.c_size_t,
             "nl_decode_workspace_bytes": ctypes.c_size_t}
 
 

@@ -974,3 +974,165 @@ extern "C" int nl_flash_attention_bwd_strided(const void* Q, const void* K, cons
   return nl::flash_bwd(Q, K, V, nl::fa::Strides{q_s, q_h, q_b}, O, dO, nl::fa::Strides{o_s, o_h, o_b}, L, D_ws, dQ,
                        dK, dV, dQacc_ws, B, H, s, d, stream);
 }
+
+// ----------------------------------------------------------------------------
+// Dtype-dispatching forms of the three reference targets.  nlearn's wrappers
+// hand `flash_attention_fwd` / `_bwd_dq` / `_bwd_dkdv` f32 operands and expect
+// f32 results (nlearn/attention.py:82-91, 97, 111-128).  For NL_F32 the
+// operands are converted to bf16 tensor-core operands in the caller's
+// workspace on `stream`, the bf16 kernels run, and the results are widened
+// back to f32; dQ is taken from the f32 accumulator (scaled) rather than from
+// its bf16 rounding.  For NL_BF16 these are the plain entry points.
+namespace nl {
+namespace fa {
+
+__global__ void cast_f32_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, long long n8) {
+  griddep_sync();
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(x)[2 * i];
+    const float4 b = reinterpret_cast<const float4*>(x)[2 * i + 1];
+    reinterpret_cast<uint4*>(y)[i] =
+        make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y), pack_bf16x2(b.z, b.w));
+  }
+}
+
+// y = scale * x, x bf16 (src_f32 == nullptr) or f32, y f32; 8 elements per thread.
+__global__ void widen_f32_kernel(const __nv_bfloat16* __restrict__ xb, const float* __restrict__ xf,
+                                 float* __restrict__ y, float scale, long long n8) {
+  griddep_sync();
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float4 a, b;
+    if (xf) {
+      a = reinterpret_cast<const float4*>(xf)[2 * i];
+      b = reinterpret_cast<const float4*>(xf)[2 * i + 1];
+    } else {
+      const uint4 v = reinterpret_cast<const uint4*>(xb)[i];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+      const float2 p0 = __bfloat1622float2(h[0]), p1 = __bfloat1622float2(h[1]);
+      const float2 p2 = __bfloat1622float2(h[2]), p3 = __bfloat1622float2(h[3]);
+      a = make_float4(p0.x, p0.y, p1.x, p1.y);
+      b = make_float4(p2.x, p2.y, p3.x, p3.y);
+    }
+    reinterpret_cast<float4*>(y)[2 * i] = make_float4(a.x * scale, a.y * scale, a.z * scale, a.w * scale);
+    reinterpret_cast<float4*>(y)[2 * i + 1] = make_float4(b.x * scale, b.y * scale, b.z * scale, b.w * scale);
+  }
+}
+
+enum { kTargetFwd = 0, kTargetBwdDq = 1, kTargetBwdDkdv = 2 };
+
+inline size_t ws_align(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Workspace carve-up: `count` bf16 [n, s, 64] tensors, then (dq target) the
+// f32 [n, s, 64] accumulator.
+size_t dt_workspace_bytes(int target, int n, int s, int d, int dtype) {
+  if (n <= 0 || s <= 0 || d != HD || (dtype != NL_F32 && dtype != NL_BF16)) return 0;
+  const size_t elems = static_cast<size_t>(n) * s * HD;
+  const size_t t16 = ws_align(elems * 2);
+  const bool f32 = dtype == NL_F32;
+  switch (target) {
+    case kTargetFwd: return f32 ? 4 * t16 : 0;
+    case kTargetBwdDq: return (f32 ? 5 * t16 : 0) + ws_align(elems * 4);
+    case kTargetBwdDkdv: return f32 ? 6 * t16 : 0;
+    default: return 0;
+  }
+}
+
+int cast_in(const void* x, __nv_bfloat16* y, long long elems, cudaStream_t stream) {
+  if (reinterpret_cast<uintptr_t>(x) & 15) return NL_ERR_ALIGN;
+  const long long n8 = elems / 8;
+  launch_kernel(cast_f32_bf16_kernel, dim3(grid_cap((n8 + 255) / 256)), dim3(256), 0, stream, 1,
+                static_cast<const float*>(x), y, n8);
+  return launch_status();
+}
+
+int widen_out(const __nv_bfloat16* xb, const float* xf, void* y, float scale, long long elems, cudaStream_t stream) {
+  if (reinterpret_cast<uintptr_t>(y) & 15) return NL_ERR_ALIGN;
+  const long long n8 = elems / 8;
+  launch_kernel(widen_f32_kernel, dim3(grid_cap((n8 + 255) / 256)), dim3(256), 0, stream, 1, xb, xf,
+                static_cast<float*>(y), scale, n8);
+  return launch_status();
+}
+
+}  // namespace fa
+}  // namespace nl
+
+extern "C" size_t nl_flash_attention_workspace_bytes(int target, int n, int s, int d, int dtype) {
+  return nl::fa::dt_workspace_bytes(target, n, s, d, dtype);
+}
+
+extern "C" int nl_flash_attention_fwd_dt(const void* Q, const void* K, const void* V, void* O, float* L, int n,
+                                         int s, int d, int dtype, void* workspace, size_t ws_bytes,
+                                         cudaStream_t stream) {
+  using namespace nl::fa;
+  if (dtype == NL_BF16) return nl_flash_attention_fwd(Q, K, V, O, L, n, s, d, stream);
+  if (dtype != NL_F32) return NL_ERR_DTYPE;
+  const size_t need = dt_workspace_bytes(kTargetFwd, n, s, d, dtype);
+  if (need == 0) return NL_ERR_SHAPE;
+  if (!workspace || ws_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255)) return NL_ERR_WORKSPACE;
+  const long long elems = static_cast<long long>(n) * s * HD;
+  const size_t t16 = ws_align(static_cast<size_t>(elems) * 2);
+  char* w = static_cast<char*>(workspace);
+  auto* qb = reinterpret_cast<__nv_bfloat16*>(w);
+  auto* kb = reinterpret_cast<__nv_bfloat16*>(w + t16);
+  auto* vb = reinterpret_cast<__nv_bfloat16*>(w + 2 * t16);
+  auto* ob = reinterpret_cast<__nv_bfloat16*>(w + 3 * t16);
+  int st;
+  if ((st = cast_in(Q, qb, elems, stream)) || (st = cast_in(K, kb, elems, stream)) ||
+      (st = cast_in(V, vb, elems, stream)))
+    return st;
+  if ((st = nl_flash_attention_fwd(qb, kb, vb, ob, L, n, s, d, stream))) return st;
+  return widen_out(ob, nullptr, O, 1.f, elems, stream);
+}
+
+extern "C" int nl_flash_attention_bwd_dq_dt(const void* Q, const void* K, const void* V, const void* dO,
+                                            const float* L, const float* D, void* dQ, int n, int s, int d, int dtype,
+                                            void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  using namespace nl::fa;
+  if (dtype != NL_F32 && dtype != NL_BF16) return NL_ERR_DTYPE;
+  const size_t need = dt_workspace_bytes(kTargetBwdDq, n, s, d, dtype);
+  if (need == 0 || !dQ) return NL_ERR_SHAPE;
+  if (!workspace || ws_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255)) return NL_ERR_WORKSPACE;
+  const long long elems = static_cast<long long>(n) * s * HD;
+  const size_t t16 = ws_align(static_cast<size_t>(elems) * 2);
+  char* w = static_cast<char*>(workspace);
+  if (dtype == NL_BF16)
+    return nl_flash_attention_bwd_dq(Q, K, V, dO, L, D, dQ, reinterpret_cast<float*>(w), n, s, d, stream);
+  auto* qb = reinterpret_cast<__nv_bfloat16*>(w);
+  auto* kb = reinterpret_cast<__nv_bfloat16*>(w + t16);
+  auto* vb = reinterpret_cast<__nv_bfloat16*>(w + 2 * t16);
+  auto* gb = reinterpret_cast<__nv_bfloat16*>(w + 3 * t16);
+  auto* dqb = reinterpret_cast<__nv_bfloat16*>(w + 4 * t16);
+  auto* acc = reinterpret_cast<float*>(w + 5 * t16);
+  int st;
+  if ((st = cast_in(Q, qb, elems, stream)) || (st = cast_in(K, kb, elems, stream)) ||
+      (st = cast_in(V, vb, elems, stream)) || (st = cast_in(dO, gb, elems, stream)))
+    return st;
+  if ((st = nl_flash_attention_bwd_dq(qb, kb, vb, gb, L, D, dqb, acc, n, s, d, stream))) return st;
+  // the accumulator holds sum_j dS_ij K_j unscaled; dQ = scale * acc in f32
+  return widen_out(nullptr, acc, dQ, 1.f / sqrtf(static_cast<float>(HD)), elems, stream);
+}
+
+extern "C" int nl_flash_attention_bwd_dkdv_dt(const void* Q, const void* K, const void* V, const void* dO,
+                                              const float* L, const float* D, void* dK, void* dV, int n, int s, int d,
+                                              int dtype, void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  using namespace nl::fa;
+  if (dtype == NL_BF16) return nl_flash_attention_bwd_dkdv(Q, K, V, dO, L, D, dK, dV, n, s, d, stream);
+  if (dtype != NL_F32) return NL_ERR_DTYPE;
+  const size_t need = dt_workspace_bytes(kTargetBwdDkdv, n, s, d, dtype);
+  if (need == 0 || !dK || !dV) return NL_ERR_SHAPE;
+  if (!workspace || ws_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255)) return NL_ERR_WORKSPACE;
+  const long long elems = static_cast<long long>(n) * s * HD;
+  const size_t t16 = ws_align(static_cast<size_t>(elems) * 2);
+  char* w = static_cast<char*>(workspace);
+  __nv_bfloat16* b[6];
+  for (int i = 0; i < 6; ++i) b[i] = reinterpret_cast<__nv_bfloat16*>(w + i * t16);
+  int st;
+  if ((st = cast_in(Q, b[0], elems, stream)) || (st = cast_in(K, b[1], elems, stream)) ||
+      (st = cast_in(V, b[2], elems, stream)) || (st = cast_in(dO, b[3], elems, stream)))
+    return st;
+  if ((st = nl_flash_attention_bwd_dkdv(b[0], b[1], b[2], b[3], L, D, b[4], b[5], n, s, d, stream))) return st;
+  if ((st = widen_out(b[4], nullptr, dK, 1.f, elems, stream))) return st;
+  return widen_out(b[5], nullptr, dV, 1.f, elems, stream);
+}

@@ -154,3 +154,63 @@ def test_strided_qkv_layout(cuda):
     assert torch.equal(to_c(O), Oc) and torch.equal(L, Lc)
     assert torch.equal(to_c(dqkv[:, :, 1]), dKc) and torch.equal(to_c(dqkv[:, :, 2]), dVc)
     assert ((to_c(dqkv[:, :, 0]).float() - dQc.float()).abs().max() <= 1e-2 * dQc.float().abs().max())
+
+
+@pytest.mark.parametrize("n,s", [(32, 512), (3, 200)])
+def test_f32_reference_targets(cuda, n, s):
+    """The three targets on what the reference's wrappers send (f32 Q, K, V,
+    dO; attention.py:82-91, 97, 111-128): f32 O, dQ, dK, dV out, converted to
+    bf16 tensor-core operands inside the library.  Checked against the f32
+    oracle on the unrounded inputs."""
+    rng = np.random.default_rng(n + s)
+    mk = lambda: rng.standard_normal((n, s, 64)).astype(np.float32)
+    Q, K, V, dO = mk(), mk(), mk(), mk()
+    t = lambda x: torch.from_numpy(x).to(cuda)
+    O, L = A.flash_attention_fwd(t(Q), t(K), t(V))
+    assert O.dtype == torch.float32 and L.dtype == torch.float32
+    D = (O * t(dO)).sum(-1)                       # attention.py:115, D computed by the caller
+    dQ = A.flash_attention_bwd_dq(t(Q), t(K), t(V), t(dO), L, D)
+    dK, dV = A.flash_attention_bwd_dkdv(t(Q), t(K), t(V), t(dO), L, D)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert dQ.dtype == dK.dtype == dV.dtype == torch.float32
+    Or, Lr = ops.attention_fwd(Q, K, V)
+    dQr, dKr, dVr, _ = ops.attention_bwd(Q, K, V, dO)
+    f = lambda x: x.cpu().numpy()
+    assert nrel(f(O), Or) < TOL and np.abs(f(L) - Lr).max() < 2e-2
+    assert nrel(f(dQ), dQr) < TOL and nrel(f(dK), dKr) < TOL and nrel(f(dV), dVr) < TOL
+
+
+def test_f32_autograd_follows_reference_rule(cuda):
+    """_attention_iree_flash with f32 inputs: the fwd target, then D =
+    rowsum(dO * O) and the dq / dkdv targets, all f32 at the boundary."""
+    torch.manual_seed(1)
+    n, s = 16, 256
+    Q, K, V = (torch.randn(n, s, 64, device=cuda).requires_grad_() for _ in range(3))
+    O = A._attention_iree_flash(Q, K, V)
+    assert O.dtype == torch.float32
+    g = torch.randn_like(O)
+    O.backward(g)
+    Qr, Kr, Vr = (x.detach().double().requires_grad_() for x in (Q, K, V))
+    Or = torch.nn.functional.scaled_dot_product_attention(Qr, Kr, Vr, is_causal=True)
+    Or.backward(g.double())
+    r = lambda a, b: ((a.double() - b).abs().max() / b.abs().max()).item()
+    assert r(O, Or) < TOL
+    assert Q.grad.dtype == torch.float32
+    assert r(Q.grad, Qr.grad) < TOL and r(K.grad, Kr.grad) < TOL and r(V.grad, Vr.grad) < TOL
+
+
+def test_dt_entry_points_reject_bad_workspace_and_dtype(cuda):
+    from nlearn_b200._lib import lib, stream_handle, STATUS
+    n, s = 2, 64
+    assert lib.nl_flash_attention_workspace_bytes(0, n, s, 64, 0) > 0
+    assert lib.nl_flash_attention_workspace_bytes(0, n, s, 64, 1) == 0
+    assert lib.nl_flash_attention_workspace_bytes(0, n, s, 32, 0) == 0
+    x = torch.zeros(n, s, 64, device=cuda)
+    L = torch.zeros(n, s, device=cuda)
+    st = lib.nl_flash_attention_fwd_dt(x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(), L.data_ptr(), n, s,
+                                       64, 0, None, 0, stream_handle())
+    assert STATUS[st] == "NL_ERR_WORKSPACE"
+    st = lib.nl_flash_attention_fwd_dt(x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(), L.data_ptr(), n, s,
+                                       64, 7, None, 0, stream_handle())
+    assert STATUS[st] == "NL_ERR_DTYPE"

@@ -1,6 +1,15 @@
 """Data-parallel step on 2 GPUs (NCCL) matches the 1-GPU step on the union of
-the two ranks' batches: the bucketed all-reduce plus per-bucket AdamW must
-produce the same weights as one AdamW over the full-batch mean gradient.
+the two ranks' batches.
+
+After one step each rank's gradient buffer holds the all-reduced mean
+gradient, which must equal the 1-GPU full-batch gradient: elementwise within
+1e-2 relative on every element whose magnitude clears 1e-2 of its tensor's
+largest, 1e-3 of the tensor's largest anywhere, and 1e-3 normwise.  Both sides
+run the same kernels; only the f32 summation order of the weight-gradient
+reductions and of the all-reduce differs.  The replicas' weights must stay
+bit-identical, and after the step's AdamW the update vector must match the
+1-GPU one within 1e-2 normwise (Adam moves near-zero-gradient elements by
+about lr in a direction set by round-off, so that check is normwise).
 Skipped when fewer than 2 GPUs are visible."""
 import os
 
@@ -10,7 +19,7 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-STEPS = 3
+STEPS = 1
 
 
 def _rank(rank, world, port, out):
@@ -25,7 +34,7 @@ def _rank(rank, world, port, out):
                  rank, world)
     losses = [tr.train_step(*tr.loader.next()) for _ in range(STEPS)]
     torch.cuda.synchronize()
-    out[rank] = (tr.P.master.cpu().numpy(), losses)
+    out[rank] = (tr.P.master.cpu().numpy(), losses, tr.P.grad.cpu().numpy())
     dist.destroy_process_group()
 
 
@@ -37,9 +46,10 @@ def test_dp2_matches_single_gpu_full_batch():
     mgr = mp.Manager()
     out = mgr.dict()
     mp.spawn(_rank, args=(2, 29600 + os.getpid() % 300, out), nprocs=2, join=True)
-    m0, l0 = out[0]
-    m1, _ = out[1]
+    m0, l0, g0 = out[0]
+    m1, _, g1 = out[1]
     assert np.array_equal(m0, m1)  # replicas stay identical
+    assert np.array_equal(g0, g1)  # both hold the same reduced gradient
     ref = Trainer(GPTConfig(), TrainConfig(batch=4, seq=128, steps=10, warmup=2), "cuda:0")
     m_init = ref.P.master.cpu().numpy()
     a, b = ZipfLoader(2, 128, 50257, 0, 0), ZipfLoader(2, 128, 50257, 0, 1)
@@ -48,9 +58,19 @@ def test_dp2_matches_single_gpu_full_batch():
         ref.train_step(np.concatenate([xa, xb]), np.concatenate([ya, yb]))
     torch.cuda.synchronize()
     mr = ref.P.master.cpu().numpy()
-    # Adam moves every element by ~lr whatever the gradient's size, so an
-    # element whose gradient is ~0 may step either way under f32 summation-order
-    # differences; compare the update vectors as a whole instead.
+    gr = ref.P.grad.cpu().numpy()
+    for name, shape, _ in ref.P.specs:
+        off, shp = ref.P.offsets[name]
+        n = int(np.prod(shp))
+        gd, gf = g0[off:off + n].astype(np.float64), gr[off:off + n].astype(np.float64)
+        top = np.abs(gf).max()
+        if top == 0:
+            assert np.abs(gd).max() == 0, name
+            continue
+        big = np.abs(gf) > 1e-2 * top
+        assert (np.abs(gd - gf)[big] <= 1e-2 * np.abs(gf)[big]).all(), name
+        assert np.abs(gd - gf).max() <= 1e-3 * top, (name, np.abs(gd - gf).max() / top)
+        assert np.linalg.norm(gd - gf) <= 1e-3 * np.linalg.norm(gf), name
     ud, ur = (m0 - m_init).astype(np.float64), (mr - m_init).astype(np.float64)
     rel = np.linalg.norm(ud - ur) / np.linalg.norm(ur)
-    assert rel < 5e-2, rel
+    assert rel < 1e-2, rel
