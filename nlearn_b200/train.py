@@ -165,6 +165,7 @@ class Trainer:
         self.loader = ZipfLoader(tcfg.batch, tcfg.seq, cfg.vocab, tcfg.seed, rank)
         self.step_idx = 0
         self.warmup = min(tcfg.warmup, tcfg.steps // 5)
+        self.tail_events = None   # set to a list to record (end of backward, end of step) events per step
 
     def lr(self, step: int) -> float:
         return lr_schedule(step, self.tcfg.peak_lr, self.warmup, self.tcfg.steps)
@@ -183,9 +184,17 @@ class Trainer:
         loss, saved = self.model.forward(tok, tgt)
         self.reducer.begin()
         self.model.backward(saved, on_grad_ready=self.reducer.ready)
+        tail = None
+        if self.tail_events is not None:  # device time of the exchange/optimizer tail after the backward
+            tail = torch.cuda.Event(enable_timing=True)
+            tail.record()
         self.reducer.finish()
         if self.reducer.optimizer is None:
             self.opt.step()
+        if tail is not None:
+            end = torch.cuda.Event(enable_timing=True)
+            end.record()
+            self.tail_events.append((tail, end))
         return loss
 
     def step_on_device(self, tok: torch.Tensor, tgt: torch.Tensor) -> torch.Tensor:
