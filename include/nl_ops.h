@@ -223,6 +223,29 @@ NL_API int nl_cast_bf16(const float* x, void* y, long long n, cudaStream_t strea
 NL_API int nl_adamw_schedule(float* hyper, int* step, float peak_lr, int warmup, int decay_steps, float end_lr,
                              float b1, float b2, cudaStream_t stream);
 
+/* Embedding-table rows for the data-parallel exchange and the optimizer (no
+ * reference counterpart: optax updates the dense table, nlearn/train.py:338).
+ * The token table's gradient is zero on every row that no token of the global
+ * batch touched; those rows can be updated (zero-gradient AdamW) as soon as
+ * the step starts, and only the touched rows are all-reduced after the
+ * backward.  Counts live in device memory, so the kernels need no host sync.
+ *   nl_rows_mark:    mark[tok[m]] = 1 for m < M (mark int32 [V], zero on entry)
+ *   nl_rows_compact: idx_on = ascending marked rows, idx_off = the others,
+ *                    counts[0] = #on, counts[1] = #off; clears mark (one CTA)
+ *   nl_rows_gather:  dst[u] = src[idx[u]] for u < min(*count, max_rows), rows of D f32
+ *   nl_rows_scatter: dst[idx[u]] = src[u]
+ *   nl_adamw_rows:   nl_adamw_step on rows idx[0 .. *count) of a [rows, D] table
+ *                    (g == NULL: zero gradient) */
+NL_API int nl_rows_mark(const int* tok, long long M, int* mark, int V, cudaStream_t stream);
+NL_API int nl_rows_compact(int* mark, int V, int* idx_on, int* idx_off, int* counts, cudaStream_t stream);
+NL_API int nl_rows_gather(const float* src, const int* idx, const int* count, int D, float* dst, int max_rows,
+                          cudaStream_t stream);
+NL_API int nl_rows_scatter(const float* src, const int* idx, const int* count, int D, float* dst, int max_rows,
+                           cudaStream_t stream);
+NL_API int nl_adamw_rows(float* p, const float* g, float* m, float* v, void* shadow_bf16, const int* idx,
+                         const int* count, int D, int max_rows, const float* hyper, float b1, float b2, float eps,
+                         float wd, cudaStream_t stream);
+
 /* ---------------------------------------------------------------- fused LM-head CE
  * Replaces the jnp-chunked `linear_cross_entropy` (nlearn/kernels/
  * cross_entropy.py:106-167; its custom_vjp 131-170): loss over

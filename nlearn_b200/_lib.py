@@ -67,6 +67,11 @@ SIGNATURES: dict[str, list] = {
     "nl_linear_ln_small": [c_void_p, c_longlong, c_void_p, c_void_p, c_float, c_void_p, c_longlong, c_void_p,
                            c_longlong, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
     "nl_cast_bf16": [c_void_p, c_void_p, c_longlong, c_void_p],
+    "nl_rows_mark": [c_void_p, c_longlong, c_void_p, c_int, c_void_p],
+    "nl_rows_compact": [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
+    "nl_rows_gather": [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p],
+    "nl_rows_scatter": [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p],
+    "nl_adamw_rows": [c_void_p] * 7 + [c_int, c_int, c_void_p, c_float, c_float, c_float, c_float, c_void_p],
     "nl_lce_workspace_bytes": [c_int, c_int, c_int],
     "nl_lce_fwd": [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t,
                    c_int, c_int, c_int, c_void_p],

@@ -322,6 +322,132 @@ __global__ void cast_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __r
   }
 }
 
+// ---------------------------------------------------------------- embedding rows
+// The token table's gradient is non-zero only on the rows of tokens that occur
+// in the (global) batch.  These kernels find those rows once per step (from
+// the token ids, known before the forward), so that the exchange and the
+// optimizer can treat the two row sets apart: rows no token touched have a
+// zero gradient on every rank and can be updated as soon as the step starts;
+// only the touched rows wait for the backward and cross NVLink.
+
+// mark[tok[m]] = 1 (mark zeroed beforehand; nl_rows_compact clears it again).
+__global__ void rows_mark_kernel(const int* __restrict__ tok, long long M, int* __restrict__ mark, int V) {
+  griddep_sync();
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < M;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int t = tok[i];
+    if (t >= 0 && t < V) mark[t] = 1;
+  }
+}
+
+// One CTA of 1024 threads: ascending lists of marked rows (idx_on) and
+// unmarked rows (idx_off), counts[0] = #on, counts[1] = #off; the marks are
+// cleared for the next step.  Thread k owns rows [k*per, (k+1)*per).
+__global__ void __launch_bounds__(1024) rows_compact_kernel(int* __restrict__ mark, int V, int* __restrict__ idx_on,
+                                                            int* __restrict__ idx_off, int* __restrict__ counts) {
+  griddep_sync();
+  __shared__ int warp_tot[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (V + 1023) / 1024;
+  const int r0 = tid * per, r1 = min(V, r0 + per);
+  int on = 0;
+  for (int r = r0; r < r1; ++r) on += mark[r] != 0;
+  // exclusive scan of `on` over the block
+  int inc = on;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) warp_tot[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    int w = warp_tot[lane];
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    warp_tot[lane] = wi - w;  // exclusive prefix of the warp totals
+  }
+  __syncthreads();
+  int pos_on = warp_tot[warp] + inc - on;
+  int pos_off = (r0 < V ? r0 : V) - pos_on;  // rows before r0 that are off
+  for (int r = r0; r < r1; ++r) {
+    if (mark[r]) {
+      idx_on[pos_on++] = r;
+      mark[r] = 0;
+    } else {
+      idx_off[pos_off++] = r;
+    }
+  }
+  if (tid == 1023) {
+    counts[0] = pos_on;
+    counts[1] = V - pos_on;
+  }
+}
+
+// dst[u, :] = src[idx[u], :] for u < *count (one warp per row, float4).
+__global__ void rows_gather_kernel(const float* __restrict__ src, const int* __restrict__ idx,
+                                   const int* __restrict__ count, int D4, float* __restrict__ dst, int max_rows) {
+  griddep_sync();
+  const int n = min(*count, max_rows);
+  const int lane = threadIdx.x & 31;
+  for (int u = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; u < n; u += (gridDim.x * blockDim.x) >> 5) {
+    const float4* s = reinterpret_cast<const float4*>(src) + static_cast<long long>(idx[u]) * D4;
+    float4* d = reinterpret_cast<float4*>(dst) + static_cast<long long>(u) * D4;
+    for (int c = lane; c < D4; c += 32) d[c] = s[c];
+  }
+}
+
+// dst[idx[u], :] = src[u, :] for u < *count.
+__global__ void rows_scatter_kernel(const float* __restrict__ src, const int* __restrict__ idx,
+                                    const int* __restrict__ count, int D4, float* __restrict__ dst, int max_rows) {
+  griddep_sync();
+  const int n = min(*count, max_rows);
+  const int lane = threadIdx.x & 31;
+  for (int u = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; u < n; u += (gridDim.x * blockDim.x) >> 5) {
+    const float4* s = reinterpret_cast<const float4*>(src) + static_cast<long long>(u) * D4;
+    float4* d = reinterpret_cast<float4*>(dst) + static_cast<long long>(idx[u]) * D4;
+    for (int c = lane; c < D4; c += 32) d[c] = s[c];
+  }
+}
+
+// AdamW (as adamw_kernel) on the rows idx[0 .. *count) of a [rows, D] table;
+// g == nullptr means a zero gradient (rows no token touched).
+__global__ void adamw_rows_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                                  float* __restrict__ v, __nv_bfloat16* __restrict__ shadow,
+                                  const int* __restrict__ idx, const int* __restrict__ count, int D4, int max_rows,
+                                  const float* __restrict__ hyper, float b1, float b2, float eps, float wd) {
+  griddep_sync();
+  const float lr = hyper[0], ibc1 = 1.f / hyper[1], ibc2 = 1.f / hyper[2];
+  const long long n = static_cast<long long>(min(*count, max_rows)) * D4;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long e = static_cast<long long>(idx[i / D4]) * D4 + i % D4;
+    float4 pp = reinterpret_cast<float4*>(p)[e];
+    const float4 gg = g ? reinterpret_cast<const float4*>(g)[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 mm = reinterpret_cast<float4*>(m)[e];
+    float4 vv = reinterpret_cast<float4*>(v)[e];
+    float* P = &pp.x;
+    const float* G = &gg.x;
+    float* Mm = &mm.x;
+    float* Vv = &vv.x;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      Mm[k] = b1 * Mm[k] + (1.f - b1) * G[k];
+      Vv[k] = b2 * Vv[k] + (1.f - b2) * G[k] * G[k];
+      const float upd = (Mm[k] * ibc1) / (sqrtf(Vv[k] * ibc2) + eps) + wd * P[k];
+      P[k] -= lr * upd;
+    }
+    reinterpret_cast<float4*>(p)[e] = pp;
+    reinterpret_cast<float4*>(m)[e] = mm;
+    reinterpret_cast<float4*>(v)[e] = vv;
+    if (shadow) reinterpret_cast<uint2*>(shadow)[e] = make_uint2(pack_bf16x2(pp.x, pp.y), pack_bf16x2(pp.z, pp.w));
+  }
+}
+
 inline int row_grid(long long M) {
   const long long warps = M;
   long long blocks = (warps * 32 + 255) / 256;
@@ -438,5 +564,59 @@ extern "C" int nl_cast_bf16(const float* x, void* y, long long n, cudaStream_t s
   const long long cap = static_cast<long long>(sm_count()) * 16;
   if (blocks > cap) blocks = cap;
   launch_kernel(ew::cast_bf16_kernel, dim3(static_cast<int>(blocks)), dim3(256), 0, stream, 1, x, static_cast<__nv_bfloat16*>(y), n4);
+  return launch_status();
+}
+
+extern "C" int nl_rows_mark(const int* tok, long long M, int* mark, int V, cudaStream_t stream) {
+  if (M <= 0 || V <= 0 || !tok || !mark) return NL_ERR_SHAPE;
+  long long blocks = (M + 255) / 256;
+  const long long cap = static_cast<long long>(sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  launch_kernel(ew::rows_mark_kernel, dim3(static_cast<int>(blocks)), dim3(256), 0, stream, 1, tok, M, mark, V);
+  return launch_status();
+}
+
+extern "C" int nl_rows_compact(int* mark, int V, int* idx_on, int* idx_off, int* counts, cudaStream_t stream) {
+  if (V <= 0 || !mark || !idx_on || !idx_off || !counts) return NL_ERR_SHAPE;
+  launch_kernel(ew::rows_compact_kernel, dim3(1), dim3(1024), 0, stream, 1, mark, V, idx_on, idx_off, counts);
+  return launch_status();
+}
+
+namespace {
+int rows_grid(int max_rows) {
+  long long blocks = (static_cast<long long>(max_rows) * 32 + 255) / 256;
+  const long long cap = static_cast<long long>(sm_count()) * 8;
+  return static_cast<int>(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+}
+}  // namespace
+
+extern "C" int nl_rows_gather(const float* src, const int* idx, const int* count, int D, float* dst, int max_rows,
+                              cudaStream_t stream) {
+  if (D <= 0 || (D & 3) || max_rows <= 0) return NL_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) return NL_ERR_ALIGN;
+  launch_kernel(ew::rows_gather_kernel, dim3(rows_grid(max_rows)), dim3(256), 0, stream, 1, src, idx, count, D / 4,
+                dst, max_rows);
+  return launch_status();
+}
+
+extern "C" int nl_rows_scatter(const float* src, const int* idx, const int* count, int D, float* dst, int max_rows,
+                               cudaStream_t stream) {
+  if (D <= 0 || (D & 3) || max_rows <= 0) return NL_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) return NL_ERR_ALIGN;
+  launch_kernel(ew::rows_scatter_kernel, dim3(rows_grid(max_rows)), dim3(256), 0, stream, 1, src, idx, count, D / 4,
+                dst, max_rows);
+  return launch_status();
+}
+
+extern "C" int nl_adamw_rows(float* p, const float* g, float* m, float* v, void* shadow_bf16, const int* idx,
+                             const int* count, int D, int max_rows, const float* hyper, float b1, float b2, float eps,
+                             float wd, cudaStream_t stream) {
+  if (D <= 0 || (D & 3) || max_rows <= 0 || !idx || !count || !hyper) return NL_ERR_SHAPE;
+  const long long n4 = static_cast<long long>(max_rows) * (D / 4);
+  long long blocks = (n4 + 255) / 256;
+  const long long cap = static_cast<long long>(sm_count()) * 16;
+  if (blocks > cap) blocks = cap;
+  launch_kernel(ew::adamw_rows_kernel, dim3(static_cast<int>(blocks)), dim3(256), 0, stream, 1, p, g, m, v,
+                static_cast<__nv_bfloat16*>(shadow_bf16), idx, count, D / 4, max_rows, hyper, b1, b2, eps, wd);
   return launch_status();
 }

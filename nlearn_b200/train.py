@@ -58,17 +58,33 @@ class ZipfLoader:
 
 # ----------------------------------------------------------------------------- DP
 class BucketReducer:
-    """All-reduce (mean) of the flat gradient buffer in contiguous buckets,
-    each launched on a communication stream as soon as the backward reports
-    every parameter in it final.  Parameters are laid out in gradient-
-    production order, so buckets complete front to back."""
+    """Gradient exchange and optimizer, bucket by bucket, overlapped with the
+    backward.
 
-    def __init__(self, params: FlatParams, bucket_bytes: int = 64 << 20, group=None, optimizer=None):
+    The flat gradient buffer is cut into contiguous buckets in gradient-
+    production order.  When the backward reports every parameter of a bucket
+    final (and its weights read for the last time), the bucket is all-reduced
+    (mean) on a side stream and, if an optimizer is attached, AdamW updates it
+    right after on the same stream, while the backward goes on.  With one rank
+    there is no exchange; the per-bucket AdamW still overlaps the backward.
+
+    The token table (``wte``) is its own bucket and is handled by rows
+    (``begin_rows``): its gradient is zero on every row that no input token of
+    the global batch touched, so those rows get their zero-gradient AdamW
+    update at the start of the step, and after the backward only the touched
+    rows are gathered, all-reduced, scattered back and updated.  The touched
+    set comes from the token ids (all-reduced across ranks), known before the
+    forward.  Results equal the dense exchange and the dense AdamW."""
+
+    def __init__(self, params: FlatParams, bucket_bytes: int = 64 << 20, group=None, optimizer=None,
+                 sparse_rows: bool | None = None):
         self.P = params
         self.optimizer = optimizer  # if set, each bucket's AdamW runs right after its all-reduce
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.use_avg = dist.is_initialized() and dist.get_backend(group) == "nccl"
+        cuda = params.device.type == "cuda"
+        self.sparse = (cuda and optimizer is not None) if sparse_rows is None else bool(sparse_rows)
         cap = max(1, bucket_bytes // 4)
         self.buckets = []  # (start, end, {names})
         cur_names, start = set(), None
@@ -76,26 +92,78 @@ class BucketReducer:
         for name, shape, _ in params.specs:
             off, shp = params.offsets[name]
             n = int(np.prod(shp))
+            if self.sparse and name == "wte" and cur_names:   # the token table is a bucket of its own
+                self.buckets.append((start, end, cur_names))
+                cur_names, start = set(), None
             if start is None:
                 start = off
             cur_names.add(name)
             end = off + n
-            if end - start >= cap:
+            if end - start >= cap or (self.sparse and name == "wte"):
                 self.buckets.append((start, end, cur_names))
                 cur_names, start = set(), None
         if cur_names:
             self.buckets.append((start, end, cur_names))
         self.owner = {n: i for i, (_, _, ns) in enumerate(self.buckets) for n in ns}
-        self.stream = torch.cuda.Stream(device=params.device) if params.device.type == "cuda" else None
+        self.stream = torch.cuda.Stream(device=params.device) if cuda else None
         self._pending = None
         self._launched = []
+        self._rows_ready = False
+        if self.sparse:
+            V, D = params.offsets["wte"][1]
+            self.V, self.D = V, D
+            dev = params.device
+            self.mark = torch.zeros(V, device=dev, dtype=torch.int32)
+            self.idx_on = torch.empty(V, device=dev, dtype=torch.int32)
+            self.idx_off = torch.empty(V, device=dev, dtype=torch.int32)
+            self.counts = torch.zeros(2, device=dev, dtype=torch.int32)
+            self.counts_host = torch.zeros(2, dtype=torch.int32).pin_memory()
+            self.counts_event = torch.cuda.Event()
+            self.rows_buf = torch.empty(V, D, device=dev, dtype=torch.float32) if self.world > 1 else None
+
+    def active(self) -> bool:
+        """Whether buckets are processed during the backward (exchange with
+        more than one rank, or the overlapped optimizer)."""
+        return self.world > 1 or self.optimizer is not None
 
     def begin(self):
         self._pending = [set(ns) for (_, _, ns) in self.buckets]
         self._launched = []
 
+    def begin_rows(self, tok: torch.Tensor):
+        """Start of a step (after the optimizer's schedule is staged): find the
+        token rows this step touches across all ranks and update the others."""
+        if not self.sparse:
+            return
+        from ._lib import check, lib, ptr
+        cur = torch.cuda.current_stream()
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        self.stream.wait_event(ev)
+        with torch.cuda.stream(self.stream):
+            h = torch.cuda.current_stream().cuda_stream
+            check(lib.nl_rows_mark(ptr(tok), tok.numel(), ptr(self.mark), self.V, h), "nl_rows_mark")
+            if self.world > 1:
+                dist.all_reduce(self.mark, op=dist.ReduceOp.MAX, group=self.group)
+            check(lib.nl_rows_compact(ptr(self.mark), self.V, ptr(self.idx_on), ptr(self.idx_off), ptr(self.counts),
+                                      h), "nl_rows_compact")
+            if self.world > 1:  # the exchange's element count is needed on the host after the backward
+                self.counts_host.copy_(self.counts, non_blocking=True)
+                self.counts_event.record()
+            self._adamw_rows(self.idx_off, self.counts[1:], None)
+        self._rows_ready = True
+
+    def _adamw_rows(self, idx, count, g):
+        from ._lib import check, lib, ptr
+        P, o = self.P, self.optimizer
+        off = P.offsets["wte"][0]
+        h = torch.cuda.current_stream().cuda_stream
+        check(lib.nl_adamw_rows(ptr(P.master[off:]), None if g is None else ptr(g), ptr(P.exp_avg[off:]),
+                                ptr(P.exp_avg_sq[off:]), ptr(P.shadow[off:]), ptr(idx), ptr(count), self.D, self.V,
+                                ptr(o.hyper), o.b1, o.b2, o.eps, o.wd, h), "nl_adamw_rows")
+
     def ready(self, name: str):
-        if self.world == 1:
+        if not self.active():
             return
         i = self.owner[name]
         self._pending[i].discard(name)
@@ -103,21 +171,45 @@ class BucketReducer:
             self._launch(i)
 
     def _launch(self, i: int):
-        start, end, _ = self.buckets[i]
-        buf = self.P.grad[start:end]
+        start, end, names = self.buckets[i]
         if self.stream is not None:
             ev = torch.cuda.Event()
             ev.record()
             self.stream.wait_event(ev)
             with torch.cuda.stream(self.stream):
-                self._allreduce(buf)
-                if self.optimizer is not None:
-                    self.optimizer.step_range(start, end)
+                self._process(start, end, names)
         else:
-            self._allreduce(buf)
-            if self.optimizer is not None:
-                self.optimizer.step_range(start, end)
+            self._process(start, end, names)
         self._launched.append(i)
+
+    def _process(self, start: int, end: int, names):
+        if self.sparse and names == {"wte"} and self._rows_ready:
+            self._process_rows()
+            return
+        buf = self.P.grad[start:end]
+        if self.world > 1:
+            self._allreduce(buf)
+        if self.optimizer is not None:
+            self.optimizer.step_range(start, end)
+
+    def _process_rows(self):
+        """The token table after the backward: touched rows only."""
+        from ._lib import check, lib, ptr
+        g = self.P.g("wte")
+        on = self.counts[:1]
+        if self.world > 1:
+            h = torch.cuda.current_stream().cuda_stream
+            self.counts_event.synchronize()      # recorded at the step's start: long complete
+            U = int(self.counts_host[0])
+            check(lib.nl_rows_gather(ptr(g), ptr(self.idx_on), ptr(on), self.D, ptr(self.rows_buf), self.V, h),
+                  "nl_rows_gather")
+            if U > 0:
+                self._allreduce(self.rows_buf[:U])
+            check(lib.nl_rows_scatter(ptr(self.rows_buf), ptr(self.idx_on), ptr(on), self.D, ptr(g), self.V, h),
+                  "nl_rows_scatter")
+        if self.optimizer is not None:
+            self._adamw_rows(self.idx_on, on, g)
+        self._rows_ready = False
 
     def _allreduce(self, buf):
         if self.use_avg:
@@ -127,7 +219,7 @@ class BucketReducer:
             buf.div_(self.world)
 
     def finish(self):
-        if self.world == 1:
+        if not self.active():
             return
         for i in range(len(self.buckets)):
             if i not in self._launched:
@@ -148,6 +240,7 @@ class TrainConfig:
     seed: int = 0
     bucket_mb: int = 64
     fused_lmhead: bool | None = None   # None: NLEARN_FUSED_LMHEAD (model.fused_lmhead_default)
+    sparse_embedding_rows: bool = True  # token-table exchange / update by touched rows (BucketReducer)
 
 
 class Trainer:
@@ -158,10 +251,14 @@ class Trainer:
         self.P = FlatParams(cfg, self.device, seed=tcfg.seed)   # same init on every rank
         self.model = GPT(cfg, self.P, fused_lmhead=tcfg.fused_lmhead)
         self.opt = AdamW(self.P, weight_decay=tcfg.weight_decay)
-        # with more than one rank the optimizer runs per bucket, overlapped with
-        # the remaining backward, right after that bucket's all-reduce
-        self.reducer = BucketReducer(self.P, tcfg.bucket_mb << 20, group,
-                                     optimizer=self.opt if world > 1 else None)
+        # the optimizer runs per bucket, overlapped with the remaining backward,
+        # right after that bucket's all-reduce (with one rank: as soon as the
+        # bucket's gradients are final); the token table by rows
+        overlap = self.device.type == "cuda" or world > 1
+        # one rank: no collective to amortise, so layer-sized buckets hide more of the optimizer
+        bucket_mb = tcfg.bucket_mb if world > 1 else min(tcfg.bucket_mb, 16)
+        self.reducer = BucketReducer(self.P, bucket_mb << 20, group, optimizer=self.opt if overlap else None,
+                                     sparse_rows=tcfg.sparse_embedding_rows and self.device.type == "cuda")
         self.loader = ZipfLoader(tcfg.batch, tcfg.seq, cfg.vocab, tcfg.seed, rank)
         self.step_idx = 0
         self.warmup = min(tcfg.warmup, tcfg.steps // 5)
@@ -181,6 +278,7 @@ class Trainer:
             self.opt.advance_on_device(self.tcfg.peak_lr, self.warmup, self.tcfg.steps, self.tcfg.peak_lr / 10)
         else:
             self.opt.set_lr(self.lr(self.step_idx))
+        self.reducer.begin_rows(tok)
         loss, saved = self.model.forward(tok, tgt)
         self.reducer.begin()
         self.model.backward(saved, on_grad_ready=self.reducer.ready)
