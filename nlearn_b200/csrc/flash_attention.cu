@@ -73,10 +73,10 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 // ====================================================================== forward
 namespace fwd {
 constexpr int kThreads = 6 * 32;
-constexpr int OFF_Q = 0;
-constexpr int OFF_K = TILE;           // 2 slots
-constexpr int OFF_V = 3 * TILE;       // 2 slots
-constexpr int OFF_BAR = 5 * TILE;
+constexpr int OFF_Q = 0;              // 2 slots (the next item's Q loads during this item)
+constexpr int OFF_K = 2 * TILE;       // 2 slots
+constexpr int OFF_V = 4 * TILE;       // 2 slots
+constexpr int OFF_BAR = 6 * TILE;
 constexpr int SMEM = OFF_BAR + 256;
 constexpr int TMEM_COLS = 256;
 constexpr int COL_S = 0, COL_O = 128, COL_P = 192;  // P: 128 bf16 per row packed in 64 columns
@@ -98,38 +98,50 @@ struct FwdParams {
   int* err;
 };
 
+// Forward work item w (0 .. n*nq-1): query tile qb = nq-1 - w/n (heaviest,
+// i.e. latest, query tiles first), head = w % n.  Round k deals items
+// k*G .. k*G+G-1 to the G persistent CTAs, forwards in even rounds and
+// backwards in odd ones.
+__device__ __forceinline__ int fwd_round_item(int k) {
+  const int G = static_cast<int>(gridDim.x), b = static_cast<int>(blockIdx.x);
+  return k * G + ((k & 1) ? G - 1 - b : b);
+}
+
+// Persistent: 2 CTAs per SM, each walking its items with TMEM allocated and
+// barriers initialised once.  Ring counters run over the CTA's whole item
+// sequence (K/V tiles jg, items it), so the next item's Q and first K/V tiles
+// load, and its first S MMA runs, while this item's softmax warps write O.
 __global__ void __launch_bounds__(fwd::kThreads, 2)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, FwdParams p) {
   using namespace fwd;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;
-  uint64_t* s_free = bars + 10;
-  uint64_t* p_full = bars + 11;
-  uint64_t* o_done = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* q_full = bars + 0;   // [2]
+  uint64_t* q_empty = bars + 2;  // [2]
+  uint64_t* k_full = bars + 4;   // [2]
+  uint64_t* k_empty = bars + 6;  // [2]
+  uint64_t* v_full = bars + 8;   // [2]
+  uint64_t* v_empty = bars + 10; // [2]
+  uint64_t* s_full = bars + 12;
+  uint64_t* s_free = bars + 13;
+  uint64_t* p_full = bars + 14;
+  uint64_t* o_done = bars + 15;
+  uint64_t* o_free = bars + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
-  // heavy (late) query tiles first
-  const int qb = p.nq - 1 - static_cast<int>(blockIdx.x) / p.n;
-  const int head = static_cast<int>(blockIdx.x) % p.n;  // = bi * H + hi
-  const int bi = head / p.H, hi = head % p.H;
-  const int nkv = qb + 1;
+  const int n_items = p.n * p.nq;
 
   if (smem_u32(smem) & 1023) {  // SW128 tiles need 1 KB alignment
     if (threadIdx.x == 0 && p.err) atomicExch(p.err, 2);
     return;
   }
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
@@ -139,6 +151,7 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
     mbar_init(s_free, 128);
     mbar_init(p_full, 128);
     mbar_init(o_done, 1);
+    mbar_init(o_free, 128);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -150,56 +163,88 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
   Abort ab{abort_flag, p.err};
   griddep_sync();
 
+  auto item_of = [&](int w, int& qb, int& head) {
+    qb = p.nq - 1 - w / p.n;
+    head = w % p.n;
+  };
+
   if (warp == 0) {
+    // ------------------------------------------------------------ TMA loads
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_expect_tx(q_full, TILE);
-      tma_load_4d(&tmQ, q_full, smem + OFF_Q, 0, qb * BQ, hi, bi);
-      for (int j = 0; j < nkv; ++j) {
-        const int slot = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&k_empty[slot], ph ^ 1, ab)) break;
-        mbar_expect_tx(&k_full[slot], TILE);
-        tma_load_4d(&tmK, &k_full[slot], smem + OFF_K + slot * TILE, 0, j * BKV, hi, bi);
-        if (!mbar_wait(&v_empty[slot], ph ^ 1, ab)) break;
-        mbar_expect_tx(&v_full[slot], TILE);
-        tma_load_4d(&tmV, &v_full[slot], smem + OFF_V + slot * TILE, 0, j * BKV, hi, bi);
+      bool ok = true;
+      int jg = 0;
+      for (int it = 0, w = fwd_round_item(0); ok && w < n_items; w = fwd_round_item(++it)) {
+        int qb, head;
+        item_of(w, qb, head);
+        const int bi = head / p.H, hi = head % p.H;
+        const int qs = it & 1;
+        if (it >= 2 && !mbar_wait(&q_empty[qs], ((it >> 1) - 1) & 1, ab)) break;
+        mbar_expect_tx(&q_full[qs], TILE);
+        tma_load_4d(&tmQ, &q_full[qs], smem + OFF_Q + qs * TILE, 0, qb * BQ, hi, bi);
+        for (int j = 0; j <= qb; ++j, ++jg) {
+          const int slot = jg & 1;
+          const uint32_t ph = (jg >> 1) & 1;
+          if (!mbar_wait(&k_empty[slot], ph ^ 1, ab)) { ok = false; break; }
+          mbar_expect_tx(&k_full[slot], TILE);
+          tma_load_4d(&tmK, &k_full[slot], smem + OFF_K + slot * TILE, 0, j * BKV, hi, bi);
+          if (!mbar_wait(&v_empty[slot], ph ^ 1, ab)) { ok = false; break; }
+          mbar_expect_tx(&v_full[slot], TILE);
+          tma_load_4d(&tmV, &v_full[slot], smem + OFF_V + slot * TILE, 0, j * BKV, hi, bi);
+        }
       }
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    // S_j+1 is issued as soon as the softmax warps have pulled S_j into
+    // registers (s_free), i.e. while softmax_j runs; the first S of the next
+    // item follows the last S of this one the same way.
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16_f32(128, 128, 0, 0);
       constexpr uint32_t idO = idesc_bf16_f32(128, 64, 0, 1);
-      const uint32_t sQ = smem_u32(smem + OFF_Q);
-      bool ok = mbar_wait(q_full, 0, ab);
-      for (int j = 0; ok && j <= nkv; ++j) {
-        if (j < nkv) {
-          const int slot = j & 1;
-          if (!mbar_wait(&k_full[slot], (j >> 1) & 1, ab)) break;
-          if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, ab)) break;
-          tc_fence_after();
-          const uint32_t sK = smem_u32(smem + OFF_K + slot * TILE);
+      bool ok = true;
+      int jg = 0;   // K/V tiles issued (S MMAs)
+      int pg = 0;   // PV MMAs issued
+      for (int it = 0, w = fwd_round_item(0); ok && w < n_items; w = fwd_round_item(++it)) {
+        int qb, head;
+        item_of(w, qb, head);
+        const int nkv = qb + 1, qs = it & 1;
+        const uint32_t sQ = smem_u32(smem + OFF_Q + qs * TILE);
+        if (!mbar_wait(&q_full[qs], (it >> 1) & 1, ab)) break;
+        for (int j = 0; j <= nkv; ++j) {
+          if (j < nkv) {
+            const int slot = jg & 1;
+            if (!mbar_wait(&k_full[slot], (jg >> 1) & 1, ab)) { ok = false; break; }
+            if (jg > 0 && !mbar_wait(s_free, (jg - 1) & 1, ab)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sK = smem_u32(smem + OFF_K + slot * TILE);
 #pragma unroll
-          for (int k = 0; k < HD / 16; ++k)
-            umma_f16_ss(tmem + COL_S, sdesc_sw128(sQ + k * 32, 16, 1024), sdesc_sw128(sK + k * 32, 16, 1024), idS,
-                        k > 0);
-          umma_commit(s_full);
-          umma_commit(&k_empty[slot]);
-        }
-        if (j > 0) {
-          const int jj = j - 1, slot = jj & 1;
-          if (!mbar_wait(p_full, jj & 1, ab)) break;
-          if (!mbar_wait(&v_full[slot], (jj >> 1) & 1, ab)) break;
-          tc_fence_after();
-          const uint32_t sV = smem_u32(smem + OFF_V + slot * TILE);
+            for (int k = 0; k < HD / 16; ++k)
+              umma_f16_ss(tmem + COL_S, sdesc_sw128(sQ + k * 32, 16, 1024), sdesc_sw128(sK + k * 32, 16, 1024), idS,
+                          k > 0);
+            umma_commit(s_full);
+            umma_commit(&k_empty[slot]);
+            if (j == nkv - 1) umma_commit(&q_empty[qs]);  // the item's last read of Q
+            ++jg;
+          }
+          if (j > 0) {
+            const int jj = j - 1, slot = pg & 1;
+            if (!mbar_wait(p_full, pg & 1, ab)) { ok = false; break; }
+            if (!mbar_wait(&v_full[slot], (pg >> 1) & 1, ab)) { ok = false; break; }
+            // the item's first PV overwrites O: the previous item's O must have been read
+            if (jj == 0 && it > 0 && !mbar_wait(o_free, (it - 1) & 1, ab)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sV = smem_u32(smem + OFF_V + slot * TILE);
 #pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk)  // P (A operand) read from TMEM, 8 columns per k-step
-            umma_f16_ts(tmem + COL_O, tmem + COL_P + kk * 8, sdesc_sw128(sV + kk * 2048, 8192, 1024), idO,
-                        (jj > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(o_done);
-          umma_commit(&v_empty[slot]);
+            for (int kk = 0; kk < BKV / 16; ++kk)  // P (A operand) read from TMEM, 8 columns per k-step
+              umma_f16_ts(tmem + COL_O, tmem + COL_P + kk * 8, sdesc_sw128(sV + kk * 2048, 8192, 1024), idO,
+                          (jj > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(o_done);
+            umma_commit(&v_empty[slot]);
+            ++pg;
+          }
         }
       }
     }
@@ -207,96 +252,112 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
     // ---------------------------------------------------------- softmax warps
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const int q = qb * BQ + r;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
-      if (!mbar_wait_warp(s_full, j & 1, ab)) { ok = false; break; }
-      tc_fence_after();
-      float sv[128];  // raw scores; the softmax scale is folded into the exponent FFMA
-      {  // the four 32-column loads of the row in flight together, one wait
-        uint32_t u0[32], u1[32], u2[32], u3[32];
-        tmem_ld32(trow + COL_S, u0);
-        tmem_ld32(trow + COL_S + 32, u1);
-        tmem_ld32(trow + COL_S + 64, u2);
-        tmem_ld32(trow + COL_S + 96, u3);
-        tmem_wait_ld_tied(u0);
-        tmem_tie(u1);
-        tmem_tie(u2);
-        tmem_tie(u3);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          sv[e] = __uint_as_float(u0[e]);
-          sv[32 + e] = __uint_as_float(u1[e]);
-          sv[64 + e] = __uint_as_float(u2[e]);
-          sv[96 + e] = __uint_as_float(u3[e]);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(s_free);
-      if (j == qb) {  // diagonal tile: key index > query index is masked
-#pragma unroll
-        for (int e = 0; e < 128; ++e)
-          if (e > r) sv[e] = -INFINITY;
-      }
-      float mt = sv[0];
-#pragma unroll
-      for (int e = 1; e < 128; ++e) mt = fmaxf(mt, sv[e]);
-      mt *= p.sl2;  // (scale > 0, so the max commutes with it)
-      // Lazy rescale: keep the running max unless the tile's max exceeds it by
-      // more than 8 (log2 units).  Then P <= 2^8 and O, l stay in f32 range,
-      // and most key tiles after the first skip the O rescale entirely.
-      const float m_new = (mt > m + 8.f) ? mt : m;
-      float lt = 0.f;
-      uint32_t pk[64];
-#pragma unroll
-      for (int e = 0; e < 64; ++e) {
-        const float a = ex2_approx(fmaf(sv[2 * e], p.sl2, -m_new));
-        const float b = ex2_approx(fmaf(sv[2 * e + 1], p.sl2, -m_new));
-        lt += a + b;
-        pk[e] = pack_bf16x2(a, b);
-      }
-      const float alpha = (j > 0) ? ex2_approx(m - m_new) : 0.f;
-      if (j > 0) {
-        // PV_{j-1} complete: P buffer free, O stable
-        if (!mbar_wait_warp(o_done, (j - 1) & 1, ab)) { ok = false; break; }
+    int jg = 0;
+    for (int it = 0, w = fwd_round_item(0); ok && w < n_items; w = fwd_round_item(++it)) {
+      int qb, head;
+      item_of(w, qb, head);
+      const int bi = head / p.H, hi = head % p.H;
+      const int nkv = qb + 1;
+      const int q = qb * BQ + r;
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < nkv; ++j, ++jg) {
+        if (!mbar_wait_warp(s_full, jg & 1, ab)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha < 1.f)) {
+        float sv[128];  // raw scores; the softmax scale is folded into the exponent FFMA
+        {  // the four 32-column loads of the row in flight together, one wait
+          uint32_t u0[32], u1[32], u2[32], u3[32];
+          tmem_ld32(trow + COL_S, u0);
+          tmem_ld32(trow + COL_S + 32, u1);
+          tmem_ld32(trow + COL_S + 64, u2);
+          tmem_ld32(trow + COL_S + 96, u3);
+          tmem_wait_ld_tied(u0);
+          tmem_tie(u1);
+          tmem_tie(u2);
+          tmem_tie(u3);
 #pragma unroll
-          {  // both halves of the O row loaded together, one wait
-            uint32_t u0[32], u1[32];
-            tmem_ld32(trow + COL_O, u0);
-            tmem_ld32(trow + COL_O + 32, u1);
-            tmem_wait_ld_tied(u0);
-            tmem_tie(u1);
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              u0[e] = __float_as_uint(__uint_as_float(u0[e]) * alpha);
-              u1[e] = __float_as_uint(__uint_as_float(u1[e]) * alpha);
-            }
-            tmem_st32(trow + COL_O, u0);
-            tmem_st32(trow + COL_O + 32, u1);
+          for (int e = 0; e < 32; ++e) {
+            sv[e] = __uint_as_float(u0[e]);
+            sv[32 + e] = __uint_as_float(u1[e]);
+            sv[64 + e] = __uint_as_float(u2[e]);
+            sv[96 + e] = __uint_as_float(u3[e]);
           }
+        }
+        tc_fence_before();
+        mbar_arrive(s_free);
+        if (j == qb) {  // diagonal tile: key index > query index is masked
+#pragma unroll
+          for (int e = 0; e < 128; ++e)
+            if (e > r) sv[e] = -INFINITY;
+        }
+        // row max as 4 independent chains (short dependency chains: one softmax
+        // warp per SM sub-partition has little else to hide latency with)
+        float mx[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) mx[k] = sv[k];
+#pragma unroll
+        for (int e = 4; e < 128; ++e) mx[e & 3] = fmaxf(mx[e & 3], sv[e]);
+        float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        mt *= p.sl2;  // (scale > 0, so the max commutes with it)
+        // Lazy rescale: keep the running max unless the tile's max exceeds it by
+        // more than 8 (log2 units).  Then P <= 2^8 and O, l stay in f32 range,
+        // and most key tiles after the first skip the O rescale entirely.
+        const float m_new = (mt > m + 8.f) ? mt : m;
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};  // row sum as 4 independent chains
+        uint32_t pk[64];
+#pragma unroll
+        for (int e = 0; e < 64; ++e) {
+          const float a = ex2_approx(fmaf(sv[2 * e], p.sl2, -m_new));
+          const float b = ex2_approx(fmaf(sv[2 * e + 1], p.sl2, -m_new));
+          ls[e & 3] += a + b;
+          pk[e] = pack_bf16x2(a, b);
+        }
+        const float lt = (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        const float alpha = (j > 0) ? ex2_approx(m - m_new) : 0.f;
+        if (j > 0) {
+          // PV_{j-1} complete: P buffer free, O stable
+          if (!mbar_wait_warp(o_done, (jg - 1) & 1, ab)) { ok = false; break; }
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, alpha < 1.f)) {
+            {  // both halves of the O row loaded together, one wait
+              uint32_t u0[32], u1[32];
+              tmem_ld32(trow + COL_O, u0);
+              tmem_ld32(trow + COL_O + 32, u1);
+              tmem_wait_ld_tied(u0);
+              tmem_tie(u1);
+#pragma unroll
+              for (int e = 0; e < 32; ++e) {
+                u0[e] = __float_as_uint(__uint_as_float(u0[e]) * alpha);
+                u1[e] = __float_as_uint(__uint_as_float(u1[e]) * alpha);
+              }
+              tmem_st32(trow + COL_O, u0);
+              tmem_st32(trow + COL_O + 32, u1);
+            }
+            tmem_wait_st();
+          }
+        }
+        // (j == 0: the previous item's last PV completed before its epilogue,
+        // so the P buffer is free)
+        l = l * alpha + lt;
+        m = m_new;
+        {  // P (bf16 pairs) into TMEM columns [COL_P, COL_P + 64) of this row's lane
+          uint32_t wv[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) wv[e] = pk[e];
+          tmem_st32(trow + COL_P, wv);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) wv[e] = pk[32 + e];
+          tmem_st32(trow + COL_P + 32, wv);
           tmem_wait_st();
         }
+        tc_fence_before();
+        mbar_arrive(p_full);
       }
-      l = l * alpha + lt;
-      m = m_new;
-      {  // P (bf16 pairs) into TMEM columns [COL_P, COL_P + 64) of this row's lane
-        uint32_t w[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) w[e] = pk[e];
-        tmem_st32(trow + COL_P, w);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) w[e] = pk[32 + e];
-        tmem_st32(trow + COL_P + 32, w);
-        tmem_wait_st();
+      if (!ok || !mbar_wait_warp(o_done, (jg - 1) & 1, ab)) {
+        ok = false;
+        break;
       }
-      tc_fence_before();
-      mbar_arrive(p_full);
-    }
-    if (ok && mbar_wait_warp(o_done, (nkv - 1) & 1, ab)) {
       tc_fence_after();
       const float inv = 1.f / l;
       uint32_t ov[32];
@@ -306,6 +367,8 @@ __global__ void __launch_bounds__(fwd::kThreads, 2)
       tmem_ld32(trow + COL_O + 32, u1);
       tmem_wait_ld_tied(u0);
       tmem_tie(u1);
+      tc_fence_before();
+      mbar_arrive(o_free);  // O read: the next item's first PV may overwrite it
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const uint32_t* u = c ? u1 : u0;
@@ -462,65 +525,94 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue
+    // Software-pipelined over the CTA's iterations g (query tiles of all its
+    // items in order): S^T / dP^T of iteration g+1 are issued as soon as the
+    // P/dS warps have pulled those of g into registers (st_free), before the
+    // dV / dK / dQ products of g, so the tensor pipe computes the next scores
+    // while the P/dS warps run the exponentials of the current ones.
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16_f32(128, 128, 0, 0);   // S^T, dP^T
       constexpr uint32_t idKV = idesc_bf16_f32(128, 64, 0, 1);   // dV, dK: B MN-major
       constexpr uint32_t idQ = idesc_bf16_f32(128, 64, 1, 1);    // dQ: A and B MN-major
       const uint32_t sDS = smem_u32(smem + OFF_DS);
-      bool ok = true;
-      int g = 0, wi = 0;
-      for (int w = bwd_round_item(0); ok && w < n_items; w = bwd_round_item(++wi)) {
-        int jb, head;
-        bwd_item(p, w, jb, head);
-        const int ks = wi & 1;
-        const uint32_t sK = smem_u32(smem + OFF_K + ks * TILE), sV = smem_u32(smem + OFF_V + ks * TILE);
-        if (!mbar_wait(&kv_full[ks], (wi >> 1) & 1, ab)) break;
-        for (int it = 0; jb + it < p.nq; ++it, ++g) {
-          const int slot = g & 1;
-          if (!mbar_wait(&qdo_full[slot], (g >> 1) & 1, ab)) { ok = false; break; }
-          if (g > 0 && !mbar_wait(st_free, (g - 1) & 1, ab)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t sQ = smem_u32(smem + OFF_Q + slot * TILE);
-          const uint32_t sDO = smem_u32(smem + OFF_DO + slot * TILE);
-#pragma unroll
-          for (int k = 0; k < HD / 16; ++k)
-            umma_f16_ss(tmem + COL_S, sdesc_sw128(sK + k * 32, 16, 1024), sdesc_sw128(sQ + k * 32, 16, 1024), idS,
-                        k > 0);
-#pragma unroll
-          for (int k = 0; k < HD / 16; ++k)
-            umma_f16_ss(tmem + COL_DP, sdesc_sw128(sV + k * 32, 16, 1024), sdesc_sw128(sDO + k * 32, 16, 1024),
-                        idS, k > 0);
-          umma_commit(s_full);
-          if (!mbar_wait(ds_full, g & 1, ab)) { ok = false; break; }
-          tc_fence_after();
-          if (p.want_dkdv) {
-            // the previous item's dV / dK must have left TMEM before they restart
-            if (it == 0 && wi > 0 && !mbar_wait(acc_free, (wi - 1) & 1, ab)) { ok = false; break; }
-            tc_fence_after();
-#pragma unroll
-            for (int kk = 0; kk < BQ / 16; ++kk) {
-              const uint32_t a_off = (kk >> 2) * 16384 + (kk & 3) * 32;
-              umma_f16_ts(tmem + COL_DV, tmem + COL_PT + kk * 8, sdesc_sw128(sDO + kk * 2048, 8192, 1024), idKV,
-                          (it > 0 || kk > 0) ? 1u : 0u);
-              umma_f16_ss(tmem + COL_DK, sdesc_sw128(sDS + a_off, 16, 1024),
-                          sdesc_sw128(sQ + kk * 2048, 8192, 1024), idKV, (it > 0 || kk > 0) ? 1u : 0u);
-            }
-          }
-          if (p.want_dq) {
-            if (g > 0 && !mbar_wait(dq_free, (g - 1) & 1, ab)) { ok = false; break; }
-            tc_fence_after();
-#pragma unroll
-            for (int kk = 0; kk < BKV / 16; ++kk)
-              umma_f16_ss(tmem + COL_DQ, sdesc_sw128(sDS + kk * 2048, 16384, 1024),
-                          sdesc_sw128(sK + kk * 2048, 8192, 1024), idQ, kk > 0 ? 1u : 0u);
-            umma_commit(dq_full);
-          }
-          umma_commit(ds_empty);
-          umma_commit(&qdo_empty[slot]);
+      // iteration cursor: item index wi, its key tile jb, query-tile offset it
+      struct Cur {
+        int wi, w, jb, it;
+      };
+      auto first_of = [&](int wi) {
+        Cur c{wi, bwd_round_item(wi), 0, 0};
+        if (c.w < n_items) {
+          int head;
+          bwd_item(p, c.w, c.jb, head);
         }
-        if (!ok) break;
-        umma_commit(&kv_empty[ks]);
-        umma_commit(acc_done);
+        return c;
+      };
+      auto issue_sdp = [&](const Cur& c, int g) -> bool {
+        const int ks = c.wi & 1, slot = g & 1;
+        if (c.it == 0 && !mbar_wait(&kv_full[ks], (c.wi >> 1) & 1, ab)) return false;
+        if (!mbar_wait(&qdo_full[slot], (g >> 1) & 1, ab)) return false;
+        if (g > 0 && !mbar_wait(st_free, (g - 1) & 1, ab)) return false;
+        tc_fence_after();
+        const uint32_t sK = smem_u32(smem + OFF_K + ks * TILE), sV = smem_u32(smem + OFF_V + ks * TILE);
+        const uint32_t sQ = smem_u32(smem + OFF_Q + slot * TILE);
+        const uint32_t sDO = smem_u32(smem + OFF_DO + slot * TILE);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k)
+          umma_f16_ss(tmem + COL_S, sdesc_sw128(sK + k * 32, 16, 1024), sdesc_sw128(sQ + k * 32, 16, 1024), idS,
+                      k > 0);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k)
+          umma_f16_ss(tmem + COL_DP, sdesc_sw128(sV + k * 32, 16, 1024), sdesc_sw128(sDO + k * 32, 16, 1024), idS,
+                      k > 0);
+        umma_commit(s_full);
+        return true;
+      };
+      Cur cur = first_of(0);
+      bool ok = cur.w < n_items && issue_sdp(cur, 0);
+      for (int g = 0; ok && cur.w < n_items; ++g) {
+        // the iteration after g
+        Cur nxt = cur;
+        if (cur.jb + cur.it + 1 < p.nq) {
+          ++nxt.it;
+        } else {
+          nxt = first_of(cur.wi + 1);
+        }
+        if (nxt.w < n_items && !issue_sdp(nxt, g + 1)) break;
+        const int ks = cur.wi & 1, slot = g & 1;
+        const uint32_t sK = smem_u32(smem + OFF_K + ks * TILE);
+        const uint32_t sQ = smem_u32(smem + OFF_Q + slot * TILE);
+        const uint32_t sDO = smem_u32(smem + OFF_DO + slot * TILE);
+        if (!mbar_wait(ds_full, g & 1, ab)) break;
+        tc_fence_after();
+        if (p.want_dkdv) {
+          // the previous item's dV / dK must have left TMEM before they restart
+          if (cur.it == 0 && cur.wi > 0 && !mbar_wait(acc_free, (cur.wi - 1) & 1, ab)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BQ / 16; ++kk) {
+            const uint32_t a_off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_f16_ts(tmem + COL_DV, tmem + COL_PT + kk * 8, sdesc_sw128(sDO + kk * 2048, 8192, 1024), idKV,
+                        (cur.it > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_ss(tmem + COL_DK, sdesc_sw128(sDS + a_off, 16, 1024), sdesc_sw128(sQ + kk * 2048, 8192, 1024),
+                        idKV, (cur.it > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        if (p.want_dq) {
+          if (g > 0 && !mbar_wait(dq_free, (g - 1) & 1, ab)) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk)
+            umma_f16_ss(tmem + COL_DQ, sdesc_sw128(sDS + kk * 2048, 16384, 1024),
+                        sdesc_sw128(sK + kk * 2048, 8192, 1024), idQ, kk > 0 ? 1u : 0u);
+          umma_commit(dq_full);
+        }
+        umma_commit(ds_empty);
+        umma_commit(&qdo_empty[slot]);
+        if (nxt.wi != cur.wi || nxt.w >= n_items) {  // last query tile of this item
+          umma_commit(&kv_empty[ks]);
+          umma_commit(acc_done);
+        }
+        cur = nxt;
       }
     }
   } else if (warp < 10) {
@@ -585,6 +677,10 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
             dcol[4 * v] = d4.x; dcol[4 * v + 1] = d4.y; dcol[4 * v + 2] = d4.z; dcol[4 * v + 3] = d4.w;
           }
           tmem_wait_ld();
+          if (c == 2 * half + 1) {  // this thread's last reads of S^T / dP^T: the MMA warp may overwrite them
+            tc_fence_before();
+            mbar_arrive(st_free);
+          }
           float pv[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) pv[e] = ex2_approx(fmaf(__uint_as_float(us[e]), p.sl2, nl[e]));
@@ -610,7 +706,6 @@ __global__ void __launch_bounds__(bwd::kThreads, 1)
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(st_free);
         fence_proxy_async_smem();
         mbar_arrive(ds_full);
       }
@@ -804,8 +899,10 @@ int flash_fwd(const void* Q, const void* K, const void* V, fa::Strides qs, void*
   p.sl2 = (1.f / sqrtf(static_cast<float>(HD))) * kLog2e;
   p.err = device_error_word();
   if ((st = set_smem(flash_fwd_kernel, fwd::SMEM))) return st;
-  const long long grid = static_cast<long long>(p.n) * p.nq;
-  if (grid > 0x7fffffffLL) return NL_ERR_SHAPE;
+  const long long items = static_cast<long long>(p.n) * p.nq;
+  if (items > 0x7fffffffLL) return NL_ERR_SHAPE;
+  const long long slots = 2LL * sm_count();  // two resident CTAs per SM
+  const long long grid = items < slots ? items : slots;
   launch_kernel(flash_fwd_kernel, dim3(static_cast<unsigned>(grid)), dim3(fwd::kThreads), fwd::SMEM, stream, 1, tq, tk, tv, p);
   return launch_status();
 }

@@ -309,27 +309,40 @@ class AdamW:
         self.hyper = torch.zeros(3, device=params.device, dtype=torch.float32)
         self._hyper_host = torch.zeros(3, dtype=torch.float32).pin_memory() if params.device.type == "cuda" \
             else torch.zeros(3)
-        self.t_dev = torch.zeros(1, device=params.device, dtype=torch.int32)  # step counter for graph replay
+        self.t_dev = torch.zeros(1, device=params.device, dtype=torch.int32)  # device step counter
+        self.t_dev_value = 0   # what t_dev holds (host view); None when unknown
 
     def set_lr(self, lr: float):
-        """Stage this step's (lr, bias corrections) into device memory."""
+        """Stage an explicit learning rate (and this step's bias corrections)
+        into device memory.  Synchronous with respect to the host buffer: the
+        copy is complete when this returns, so a host that runs ahead of the
+        device cannot overwrite a value still waiting to be copied (the
+        training step itself uses advance_on_device, with no host copy)."""
         self.t += 1
         h = self._hyper_host
         h[0] = lr
         h[1] = 1 - self.b1 ** self.t
         h[2] = 1 - self.b2 ** self.t
         self.hyper.copy_(h, non_blocking=True)
+        torch.cuda.current_stream().synchronize() if self.hyper.is_cuda else None
+        self.t_dev_value = None  # the device counter no longer follows t
 
     def advance_on_device(self, peak_lr: float, warmup: int, decay_steps: int, end_lr: float):
-        """set_lr for CUDA-graph replay: a one-thread kernel advances the device
-        step counter and writes the schedule's lr and the bias corrections
-        (the counter must equal ``t`` before the first replay: sync_device_step)."""
+        """One step of the schedule on the device: a one-thread kernel advances
+        the device step counter and writes the warmup-cosine lr and the bias
+        corrections into ``hyper`` (no host-to-device copy, so eager steps can
+        run ahead of the device and a captured CUDA graph replays it)."""
+        if self.t_dev_value != self.t:
+            self.sync_device_step()
         self.t += 1
         check(lib.nl_adamw_schedule(ptr(self.hyper), ptr(self.t_dev), peak_lr, warmup, decay_steps, end_lr, self.b1,
                                     self.b2, stream_handle()), "nl_adamw_schedule")
+        self.t_dev_value = self.t
 
     def sync_device_step(self):
+        """Set the device step counter to ``t`` (after a resume, or set_lr)."""
         self.t_dev.fill_(self.t)
+        self.t_dev_value = self.t
 
     def step(self):
         self.step_range(0, self.P.numel)

@@ -72,12 +72,15 @@ class BucketReducer:
     (``begin_rows``): its gradient is zero on every row that no input token of
     the global batch touched, so those rows get their zero-gradient AdamW
     update at the start of the step, and after the backward only the touched
-    rows are gathered, all-reduced, scattered back and updated.  The touched
-    set comes from the token ids (all-reduced across ranks), known before the
-    forward.  Results equal the dense exchange and the dense AdamW."""
+    rows are updated.  The touched set comes from the token ids (all-reduced
+    across ranks), known before the forward.  With ``compact_exchange`` only
+    the touched rows are gathered, all-reduced and scattered back (fewer bytes
+    over NVLink at a host wait for their count); otherwise the whole table
+    gradient is all-reduced.  Results equal the dense exchange and the dense
+    AdamW."""
 
     def __init__(self, params: FlatParams, bucket_bytes: int = 64 << 20, group=None, optimizer=None,
-                 sparse_rows: bool | None = None):
+                 sparse_rows: bool | None = None, compact_exchange: bool = False):
         self.P = params
         self.optimizer = optimizer  # if set, each bucket's AdamW runs right after its all-reduce
         self.group = group
@@ -85,6 +88,12 @@ class BucketReducer:
         self.use_avg = dist.is_initialized() and dist.get_backend(group) == "nccl"
         cuda = params.device.type == "cuda"
         self.sparse = (cuda and optimizer is not None) if sparse_rows is None else bool(sparse_rows)
+        # all-reduce only the touched rows (needs their count on the host, read
+        # after the backward: a host wait on the step's start, which stalls a
+        # host that is not far ahead of the device); otherwise the whole table
+        # gradient is all-reduced (zero on untouched rows) and only the AdamW
+        # is split by rows
+        self.compact = self.sparse and compact_exchange and self.world > 1
         cap = max(1, bucket_bytes // 4)
         self.buckets = []  # (start, end, {names})
         cur_names, start = set(), None
@@ -119,7 +128,7 @@ class BucketReducer:
             self.counts = torch.zeros(2, device=dev, dtype=torch.int32)
             self.counts_host = torch.zeros(2, dtype=torch.int32).pin_memory()
             self.counts_event = torch.cuda.Event()
-            self.rows_buf = torch.empty(V, D, device=dev, dtype=torch.float32) if self.world > 1 else None
+            self.rows_buf = torch.empty(V, D, device=dev, dtype=torch.float32) if self.compact else None
 
     def active(self) -> bool:
         """Whether buckets are processed during the backward (exchange with
@@ -147,7 +156,7 @@ class BucketReducer:
                 dist.all_reduce(self.mark, op=dist.ReduceOp.MAX, group=self.group)
             check(lib.nl_rows_compact(ptr(self.mark), self.V, ptr(self.idx_on), ptr(self.idx_off), ptr(self.counts),
                                       h), "nl_rows_compact")
-            if self.world > 1:  # the exchange's element count is needed on the host after the backward
+            if self.compact:  # the exchange's element count is needed on the host after the backward
                 self.counts_host.copy_(self.counts, non_blocking=True)
                 self.counts_event.record()
             self._adamw_rows(self.idx_off, self.counts[1:], None)
@@ -197,7 +206,9 @@ class BucketReducer:
         from ._lib import check, lib, ptr
         g = self.P.g("wte")
         on = self.counts[:1]
-        if self.world > 1:
+        if self.world > 1 and not self.compact:
+            self._allreduce(g.view(-1))
+        elif self.world > 1:
             h = torch.cuda.current_stream().cuda_stream
             self.counts_event.synchronize()      # recorded at the step's start: long complete
             U = int(self.counts_host[0])
@@ -240,7 +251,8 @@ class TrainConfig:
     seed: int = 0
     bucket_mb: int = 64
     fused_lmhead: bool | None = None   # None: NLEARN_FUSED_LMHEAD (model.fused_lmhead_default)
-    sparse_embedding_rows: bool = True  # token-table exchange / update by touched rows (BucketReducer)
+    sparse_embedding_rows: bool = True  # token-table AdamW by rows: untouched rows at the step's start
+    compact_embedding_exchange: bool = False  # and all-reduce only the touched rows (host waits for their count)
 
 
 class Trainer:
@@ -258,7 +270,8 @@ class Trainer:
         # one rank: no collective to amortise, so layer-sized buckets hide more of the optimizer
         bucket_mb = tcfg.bucket_mb if world > 1 else min(tcfg.bucket_mb, 16)
         self.reducer = BucketReducer(self.P, bucket_mb << 20, group, optimizer=self.opt if overlap else None,
-                                     sparse_rows=tcfg.sparse_embedding_rows and self.device.type == "cuda")
+                                     sparse_rows=tcfg.sparse_embedding_rows and self.device.type == "cuda",
+                                     compact_exchange=tcfg.compact_embedding_exchange)
         self.loader = ZipfLoader(tcfg.batch, tcfg.seq, cfg.vocab, tcfg.seed, rank)
         self.step_idx = 0
         self.warmup = min(tcfg.warmup, tcfg.steps // 5)
@@ -272,12 +285,11 @@ class Trainer:
         tgt = torch.as_tensor(targets, device=self.device)
         return tok, tgt
 
-    def _step_body(self, tok: torch.Tensor, tgt: torch.Tensor, device_schedule: bool = False) -> torch.Tensor:
+    def _step_body(self, tok: torch.Tensor, tgt: torch.Tensor) -> torch.Tensor:
         self.P.grad.zero_()
-        if device_schedule:
-            self.opt.advance_on_device(self.tcfg.peak_lr, self.warmup, self.tcfg.steps, self.tcfg.peak_lr / 10)
-        else:
-            self.opt.set_lr(self.lr(self.step_idx))
+        # the schedule (optax warmup_cosine_decay, nlearn/train.py:487-505) is
+        # evaluated on the device: no per-step host copy for the host to race
+        self.opt.advance_on_device(self.tcfg.peak_lr, self.warmup, self.tcfg.steps, self.tcfg.peak_lr / 10)
         self.reducer.begin_rows(tok)
         loss, saved = self.model.forward(tok, tgt)
         self.reducer.begin()
@@ -321,25 +333,25 @@ class Trainer:
         n0 = _lib.lib.nl_launch_count()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            self._gloss = self._step_body(self._gtok, self._gtgt, device_schedule=True)
+            self._gloss = self._step_body(self._gtok, self._gtgt)
         self.opt.t = t0  # capture runs nothing; the counter advances per replay
+        self.opt.t_dev_value = t0
         self.graph_launches = _lib.lib.nl_launch_count() - n0
         self._graph = g
-        self._graph_t = t0
         return self.graph_launches
 
     def step_graphed(self, tok: torch.Tensor, tgt: torch.Tensor) -> torch.Tensor:
         """Replay the captured step on this batch (device tensors, or pinned
         host tensors copied in asynchronously); returns the static loss tensor,
         valid until the next replay."""
-        if self._graph_t != self.opt.t:  # eager steps or a resume since the last replay
+        if self.opt.t_dev_value != self.opt.t:  # a resume or set_lr since the last step
             self.opt.sync_device_step()
         self._gtok.copy_(tok, non_blocking=True)
         self._gtgt.copy_(tgt, non_blocking=True)
         self._graph.replay()
         self.opt.t += 1
+        self.opt.t_dev_value = self.opt.t
         self.step_idx += 1
-        self._graph_t = self.opt.t
         return self._gloss
 
     def train_step(self, inputs: np.ndarray, targets: np.ndarray) -> float:

