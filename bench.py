@@ -709,7 +709,7 @@ def main():
             "roofline_lm_head": {"bound": "tensor", "kernel": "LM-head forward GEMM (nl_lce_fwd, M16384 N50257 K512)",
                                  "achieved": achieved_head, "peak": sustained, "unit": "TFLOP/s",
                                  "frac": achieved_head / sustained, "peak_source": f"{src} bf16_tflops_sustained",
-                                 "traffic": traffic_from("gemm_lce_head_fwd_M4096.md",
+                                 "traffic": traffic_from("gemm_lce_head_fwd_M16384.md",
                                                          "lce_head_gemm_bytes_per_launch"),
                                  "avg_launch_ms": head_avg_ms},
             "strong": strong,

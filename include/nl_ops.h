@@ -211,9 +211,11 @@ NL_API int nl_layernorm_bwd(const void* dy, const void* x, const float* mean, co
 NL_API int nl_colsum_bf16(const void* x, float* out, int M, int N, cudaStream_t stream);
 /* AdamW on a flat f32 buffer (optax.adamw semantics); hyper = device
  * f32[3] {lr, 1-b1^t, 1-b2^t}; also writes the bf16 compute copy if non-NULL.
- * n % 4 == 0. */
-NL_API int nl_adamw_step(float* p, const float* g, float* m, float* v, void* shadow_bf16, long long n,
-                         const float* hyper, float b1, float b2, float eps, float wd, cudaStream_t stream);
+ * zero_grad != 0 clears g after reading it (the next step's accumulating
+ * gradient kernels then need no separate zeroing pass).  n % 4 == 0. */
+NL_API int nl_adamw_step(float* p, float* g, float* m, float* v, void* shadow_bf16, long long n,
+                         const float* hyper, float b1, float b2, float eps, float wd, int zero_grad,
+                         cudaStream_t stream);
 NL_API int nl_cast_bf16(const float* x, void* y, long long n, cudaStream_t stream);
 /* Advance the optimizer step on the device (for CUDA-graph replay): t =
  * ++(*step) (device int32), then hyper[0] = warmup-cosine learning rate at
@@ -231,20 +233,21 @@ NL_API int nl_adamw_schedule(float* hyper, int* step, float peak_lr, int warmup,
  * backward.  Counts live in device memory, so the kernels need no host sync.
  *   nl_rows_mark:    mark[tok[m]] = 1 for m < M (mark int32 [V], zero on entry)
  *   nl_rows_compact: idx_on = ascending marked rows, idx_off = the others,
- *                    counts[0] = #on, counts[1] = #off; clears mark (one CTA)
+ *                    counts[0] = #on, counts[1] = #off; clears mark.  counts
+ *                    holds 2 + ceil(V / 1024) int32 (the rest is scratch)
  *   nl_rows_gather:  dst[u] = src[idx[u]] for u < min(*count, max_rows), rows of D f32
  *   nl_rows_scatter: dst[idx[u]] = src[u]
  *   nl_adamw_rows:   nl_adamw_step on rows idx[0 .. *count) of a [rows, D] table
- *                    (g == NULL: zero gradient) */
+ *                    (g == NULL: zero gradient; zero_grad clears those rows of g) */
 NL_API int nl_rows_mark(const int* tok, long long M, int* mark, int V, cudaStream_t stream);
 NL_API int nl_rows_compact(int* mark, int V, int* idx_on, int* idx_off, int* counts, cudaStream_t stream);
 NL_API int nl_rows_gather(const float* src, const int* idx, const int* count, int D, float* dst, int max_rows,
                           cudaStream_t stream);
 NL_API int nl_rows_scatter(const float* src, const int* idx, const int* count, int D, float* dst, int max_rows,
                            cudaStream_t stream);
-NL_API int nl_adamw_rows(float* p, const float* g, float* m, float* v, void* shadow_bf16, const int* idx,
+NL_API int nl_adamw_rows(float* p, float* g, float* m, float* v, void* shadow_bf16, const int* idx,
                          const int* count, int D, int max_rows, const float* hyper, float b1, float b2, float eps,
-                         float wd, cudaStream_t stream);
+                         float wd, int zero_grad, cudaStream_t stream);
 
 /* ---------------------------------------------------------------- fused LM-head CE
  * Replaces the jnp-chunked `linear_cross_entropy` (nlearn/kernels/

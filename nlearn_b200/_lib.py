@@ -55,7 +55,7 @@ SIGNATURES: dict[str, list] = {
     "nl_layernorm_fwd": [c_void_p] * 6 + [c_int, c_int, c_float, c_void_p],
     "nl_layernorm_bwd": [c_void_p] * 9 + [c_int, c_int, c_int, c_void_p],
     "nl_colsum_bf16": [c_void_p, c_void_p, c_int, c_int, c_void_p],
-    "nl_adamw_step": [c_void_p] * 5 + [c_longlong, c_void_p, c_float, c_float, c_float, c_float, c_void_p],
+    "nl_adamw_step": [c_void_p] * 5 + [c_longlong, c_void_p, c_float, c_float, c_float, c_float, c_int, c_void_p],
     "nl_adamw_schedule": [c_void_p, c_void_p, c_float, c_int, c_int, c_float, c_float, c_float, c_void_p],
     "nl_decode_embed": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p],
     "nl_decode_workspace_bytes": [c_int, c_int, c_int],
@@ -71,7 +71,8 @@ SIGNATURES: dict[str, list] = {
     "nl_rows_compact": [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
     "nl_rows_gather": [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p],
     "nl_rows_scatter": [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p],
-    "nl_adamw_rows": [c_void_p] * 7 + [c_int, c_int, c_void_p, c_float, c_float, c_float, c_float, c_void_p],
+    "nl_adamw_rows": [c_void_p] * 7 + [c_int, c_int, c_void_p, c_float, c_float, c_float, c_float, c_int,
+                                       c_void_p],
     "nl_lce_workspace_bytes": [c_int, c_int, c_int],
     "nl_lce_fwd": [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t,
                    c_int, c_int, c_int, c_void_p],

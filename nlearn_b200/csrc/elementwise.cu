@@ -259,9 +259,10 @@ __global__ void colsum_kernel(const __nv_bfloat16* __restrict__ x, float* out, i
 // and the bf16 compute copy is rewritten from the updated master.
 // hyper[0..2] = lr, bc1, bc2 live in device memory so that a captured CUDA
 // graph picks up each step's schedule value.
-__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+__global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ shadow, long long n4,
-                             const float* __restrict__ hyper, float b1, float b2, float eps, float wd) {
+                             const float* __restrict__ hyper, float b1, float b2, float eps, float wd,
+                             int zero_grad) {
   griddep_sync();
   const float lr = hyper[0], bc1 = hyper[1], bc2 = hyper[2];
   const float ibc1 = 1.f / bc1, ibc2 = 1.f / bc2;
@@ -269,6 +270,7 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     float4 pp = reinterpret_cast<float4*>(p)[i];
     const float4 gg = reinterpret_cast<const float4*>(g)[i];
+    if (zero_grad) reinterpret_cast<float4*>(g)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     float4 mm = reinterpret_cast<float4*>(m)[i];
     float4 vv = reinterpret_cast<float4*>(v)[i];
     float* P = &pp.x;
@@ -340,51 +342,84 @@ __global__ void rows_mark_kernel(const int* __restrict__ tok, long long M, int* 
   }
 }
 
-// One CTA of 1024 threads: ascending lists of marked rows (idx_on) and
-// unmarked rows (idx_off), counts[0] = #on, counts[1] = #off; the marks are
-// cleared for the next step.  Thread k owns rows [k*per, (k+1)*per).
-__global__ void __launch_bounds__(1024) rows_compact_kernel(int* __restrict__ mark, int V, int* __restrict__ idx_on,
-                                                            int* __restrict__ idx_off, int* __restrict__ counts) {
-  griddep_sync();
-  __shared__ int warp_tot[32];
+// Compaction in two passes over chunks of 1024 rows (one CTA per chunk,
+// coalesced reads): rows_count_kernel writes each chunk's number of marked
+// rows; rows_list_kernel turns the preceding chunks' counts and a block-wide
+// ballot scan into positions and writes ascending lists of marked rows
+// (idx_on) and unmarked rows (idx_off), counts[0] = #on, counts[1] = #off, and
+// clears the marks for the next step.  The lists are the same on every rank
+// for the same marks (deterministic order).
+__device__ __forceinline__ int block_ballot_scan(bool on, int* warp_tot, int& total) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int per = (V + 1023) / 1024;
-  const int r0 = tid * per, r1 = min(V, r0 + per);
-  int on = 0;
-  for (int r = r0; r < r1; ++r) on += mark[r] != 0;
-  // exclusive scan of `on` over the block
-  int inc = on;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, inc, o);
-    if (lane >= o) inc += y;
-  }
-  if (lane == 31) warp_tot[warp] = inc;
+  const unsigned b = __ballot_sync(0xffffffffu, on);
+  const int before_in_warp = __popc(b & ((1u << lane) - 1u));
+  if (lane == 0) warp_tot[warp] = __popc(b);
   __syncthreads();
   if (warp == 0) {
-    int w = warp_tot[lane];
-    int wi = w;
+    const int w = warp_tot[lane];
+    int inc = w;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, wi, o);
-      if (lane >= o) wi += y;
+      const int y = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += y;
     }
-    warp_tot[lane] = wi - w;  // exclusive prefix of the warp totals
+    warp_tot[lane] = inc - w;
+    if (lane == 31) warp_tot[32] = inc;
   }
   __syncthreads();
-  int pos_on = warp_tot[warp] + inc - on;
-  int pos_off = (r0 < V ? r0 : V) - pos_on;  // rows before r0 that are off
-  for (int r = r0; r < r1; ++r) {
-    if (mark[r]) {
-      idx_on[pos_on++] = r;
-      mark[r] = 0;
-    } else {
-      idx_off[pos_off++] = r;
+  total = warp_tot[32];
+  return warp_tot[warp] + before_in_warp;
+}
+
+__global__ void __launch_bounds__(1024) rows_count_kernel(const int* __restrict__ mark, int V,
+                                                          int* __restrict__ chunk_on) {
+  griddep_sync();
+  __shared__ int warp_tot[33];
+  const int r = blockIdx.x * 1024 + threadIdx.x;
+  int total;
+  block_ballot_scan(r < V && mark[r] != 0, warp_tot, total);
+  if (threadIdx.x == 0) chunk_on[blockIdx.x] = total;
+}
+
+__global__ void __launch_bounds__(1024) rows_list_kernel(int* __restrict__ mark, int V,
+                                                         const int* __restrict__ chunk_on, int* __restrict__ idx_on,
+                                                         int* __restrict__ idx_off, int* __restrict__ counts) {
+  griddep_sync();
+  __shared__ int warp_tot[33];
+  __shared__ int base_s[2];
+  if (threadIdx.x < 32) {  // marked rows in the chunks before this one, and in all chunks
+    int before = 0, all = 0;
+    for (int c = threadIdx.x; c < gridDim.x; c += 32) {
+      const int v = chunk_on[c];
+      all += v;
+      before += (c < static_cast<int>(blockIdx.x)) ? v : 0;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      before += __shfl_xor_sync(0xffffffffu, before, o);
+      all += __shfl_xor_sync(0xffffffffu, all, o);
+    }
+    if (threadIdx.x == 0) {
+      base_s[0] = before;
+      base_s[1] = all;
     }
   }
-  if (tid == 1023) {
-    counts[0] = pos_on;
-    counts[1] = V - pos_on;
+  const int r = blockIdx.x * 1024 + threadIdx.x;
+  const bool on = r < V && mark[r] != 0;
+  int total;
+  const int pos = block_ballot_scan(on, warp_tot, total);  // (its barriers also publish base_s)
+  const int on_before = base_s[0] + pos;
+  if (r < V) {
+    if (on) {
+      idx_on[on_before] = r;
+      mark[r] = 0;
+    } else {
+      idx_off[r - on_before] = r;  // rows before r that are off
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    counts[0] = base_s[1];
+    counts[1] = V - base_s[1];
   }
 }
 
@@ -416,10 +451,11 @@ __global__ void rows_scatter_kernel(const float* __restrict__ src, const int* __
 
 // AdamW (as adamw_kernel) on the rows idx[0 .. *count) of a [rows, D] table;
 // g == nullptr means a zero gradient (rows no token touched).
-__global__ void adamw_rows_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+__global__ void adamw_rows_kernel(float* __restrict__ p, float* __restrict__ g, float* __restrict__ m,
                                   float* __restrict__ v, __nv_bfloat16* __restrict__ shadow,
                                   const int* __restrict__ idx, const int* __restrict__ count, int D4, int max_rows,
-                                  const float* __restrict__ hyper, float b1, float b2, float eps, float wd) {
+                                  const float* __restrict__ hyper, float b1, float b2, float eps, float wd,
+                                  int zero_grad) {
   griddep_sync();
   const float lr = hyper[0], ibc1 = 1.f / hyper[1], ibc2 = 1.f / hyper[2];
   const long long n = static_cast<long long>(min(*count, max_rows)) * D4;
@@ -428,6 +464,7 @@ __global__ void adamw_rows_kernel(float* __restrict__ p, const float* __restrict
     const long long e = static_cast<long long>(idx[i / D4]) * D4 + i % D4;
     float4 pp = reinterpret_cast<float4*>(p)[e];
     const float4 gg = g ? reinterpret_cast<const float4*>(g)[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (g && zero_grad) reinterpret_cast<float4*>(g)[e] = make_float4(0.f, 0.f, 0.f, 0.f);
     float4 mm = reinterpret_cast<float4*>(m)[e];
     float4 vv = reinterpret_cast<float4*>(v)[e];
     float* P = &pp.x;
@@ -536,8 +573,9 @@ extern "C" int nl_colsum_bf16(const void* x, float* out, int M, int N, cudaStrea
   return launch_status();
 }
 
-extern "C" int nl_adamw_step(float* p, const float* g, float* m, float* v, void* shadow_bf16, long long n,
-                             const float* hyper, float b1, float b2, float eps, float wd, cudaStream_t stream) {
+extern "C" int nl_adamw_step(float* p, float* g, float* m, float* v, void* shadow_bf16, long long n,
+                             const float* hyper, float b1, float b2, float eps, float wd, int zero_grad,
+                             cudaStream_t stream) {
   if (n <= 0 || (n & 3)) return NL_ERR_SHAPE;
   const long long n4 = n / 4;
   long long blocks = (n4 + 255) / 256;
@@ -545,7 +583,7 @@ extern "C" int nl_adamw_step(float* p, const float* g, float* m, float* v, void*
   if (blocks > cap) blocks = cap;
   launch_kernel(ew::adamw_kernel, dim3(static_cast<int>(blocks)), dim3(256), 0, stream, 1, p, g, m, v,
                                                                    static_cast<__nv_bfloat16*>(shadow_bf16), n4,
-                                                                   hyper, b1, b2, eps, wd);
+                                                                   hyper, b1, b2, eps, wd, zero_grad);
   return launch_status();
 }
 
@@ -578,7 +616,15 @@ extern "C" int nl_rows_mark(const int* tok, long long M, int* mark, int V, cudaS
 
 extern "C" int nl_rows_compact(int* mark, int V, int* idx_on, int* idx_off, int* counts, cudaStream_t stream) {
   if (V <= 0 || !mark || !idx_on || !idx_off || !counts) return NL_ERR_SHAPE;
-  launch_kernel(ew::rows_compact_kernel, dim3(1), dim3(1024), 0, stream, 1, mark, V, idx_on, idx_off, counts);
+  const int chunks = (V + 1023) / 1024;
+  // counts[2 .. 2 + chunks): the marked-row count of each 1024-row chunk
+  int* chunk_on = counts + 2;
+  launch_kernel(ew::rows_count_kernel, dim3(chunks), dim3(1024), 0, stream, 1, static_cast<const int*>(mark), V,
+                chunk_on);
+  int st = launch_status();
+  if (st) return st;
+  launch_kernel(ew::rows_list_kernel, dim3(chunks), dim3(1024), 0, stream, 1, mark, V,
+                static_cast<const int*>(chunk_on), idx_on, idx_off, counts);
   return launch_status();
 }
 
@@ -608,15 +654,16 @@ extern "C" int nl_rows_scatter(const float* src, const int* idx, const int* coun
   return launch_status();
 }
 
-extern "C" int nl_adamw_rows(float* p, const float* g, float* m, float* v, void* shadow_bf16, const int* idx,
+extern "C" int nl_adamw_rows(float* p, float* g, float* m, float* v, void* shadow_bf16, const int* idx,
                              const int* count, int D, int max_rows, const float* hyper, float b1, float b2, float eps,
-                             float wd, cudaStream_t stream) {
+                             float wd, int zero_grad, cudaStream_t stream) {
   if (D <= 0 || (D & 3) || max_rows <= 0 || !idx || !count || !hyper) return NL_ERR_SHAPE;
   const long long n4 = static_cast<long long>(max_rows) * (D / 4);
   long long blocks = (n4 + 255) / 256;
   const long long cap = static_cast<long long>(sm_count()) * 16;
   if (blocks > cap) blocks = cap;
   launch_kernel(ew::adamw_rows_kernel, dim3(static_cast<int>(blocks)), dim3(256), 0, stream, 1, p, g, m, v,
-                static_cast<__nv_bfloat16*>(shadow_bf16), idx, count, D / 4, max_rows, hyper, b1, b2, eps, wd);
+                static_cast<__nv_bfloat16*>(shadow_bf16), idx, count, D / 4, max_rows, hyper, b1, b2, eps, wd,
+                zero_grad);
   return launch_status();
 }

@@ -57,6 +57,7 @@ struct Params {
   int tma_out;          // 1: outputs leave through staged TMA stores (tmC / tmX valid)
   int group_m;          // M tiles per raster group
   int col_offset;       // global vocab index of this launch's column 0
+  int stream_k;         // 1: workers own equal contiguous ranges of (tile, k-block) iterations
 };
 
 template <int BN>
@@ -93,6 +94,47 @@ __device__ __forceinline__ void decode_unit(const Params& p, int u, int& mb, int
   const int r = t - g * per_group;
   mb = first_m + r % gsz;
   nb = r / gsz;
+}
+
+// A CTA's (or CTA pair's) sequence of work: tiles, each with a k-block range.
+// Unit mode: units u = worker, worker + workers, ... (tiles x split-K parts).
+// Stream-K mode (p.stream_k, accumulating epilogue only): worker w owns the
+// contiguous range [w T / W, (w+1) T / W) of the T = tiles x num_kb
+// (tile, k-block) iterations, cut at tile boundaries, so every worker does the
+// same number of k-blocks whatever the tile count; the partial tiles combine
+// through the epilogue's reduce-adds.  Every role of a CTA walks the same
+// sequence.
+struct Work {
+  long long it, end;  // stream-K
+  int u, stride;      // unit mode
+};
+__device__ __forceinline__ Work work_begin(const Params& p, int worker, int workers) {
+  Work w{0, 0, worker, workers};
+  if (p.stream_k) {
+    const long long T = static_cast<long long>(p.tiles_m) * p.tiles_n * p.num_kb;
+    w.it = T * worker / workers;
+    w.end = T * (worker + 1) / workers;
+  }
+  return w;
+}
+__device__ __forceinline__ bool work_next(const Params& p, Work& w, int& mb, int& nb, int& kb0, int& kb1) {
+  int sk;
+  if (p.stream_k) {
+    if (w.it >= w.end) return false;
+    const int tile = static_cast<int>(w.it / p.num_kb);
+    kb0 = static_cast<int>(w.it - static_cast<long long>(tile) * p.num_kb);
+    const long long left = w.end - w.it;
+    kb1 = (left < p.num_kb - kb0) ? kb0 + static_cast<int>(left) : p.num_kb;
+    w.it += kb1 - kb0;
+    decode_unit(p, tile, mb, nb, sk);
+    return true;
+  }
+  if (w.u >= p.tiles_m * p.tiles_n * p.split_k) return false;
+  decode_unit(p, w.u, mb, nb, sk);
+  kb0 = sk * p.kb_per_split;
+  kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+  w.u += w.stride;
+  return true;
 }
 
 constexpr float kLog2e = 1.4426950408889634f;
@@ -250,7 +292,7 @@ __device__ __forceinline__ void epi_chunk(const Params& p, int row, int col0, fl
   if (epi == NL_EPI_ACCUM) {
     float* cf = reinterpret_cast<float*>(p.C) + off;
     const bool vec = full && ((p.ldc & 3) == 0);
-    if (p.split_k > 1) {
+    if (p.split_k > 1 || p.stream_k) {
       if (vec) {
 #pragma unroll
         for (int j = 0; j < 8; ++j)
@@ -451,7 +493,6 @@ __device__ __forceinline__ void epilogue_role(const Params& p, uint32_t tmem_bas
                                               const CUtensorMap* tmX, uint8_t* staging) {
   uint8_t* slot = staging + (warp_id() - 2) * 4096;
   const int warp = warp_id(), lane = lane_id();
-  const int num_units = p.tiles_m * p.tiles_n * p.split_k;
   const int cta_unit0 = remote ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int cta_stride = remote ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
   const int q = warp & 3;             // TMEM lane quarter this warp may access
@@ -462,9 +503,9 @@ __device__ __forceinline__ void epilogue_role(const Params& p, uint32_t tmem_bas
   int acc = 0;
   uint32_t acc_ph = 0;
   uint32_t nblk = 0;
-  for (int u = cta_unit0; half < split && u < num_units; u += cta_stride) {
-    int mb, nb, sk;
-    decode_unit(p, u, mb, nb, sk);
+  Work wk = work_begin(p, cta_unit0, cta_stride);
+  int mb, nb, kb0, kb1;
+  while (half < split && work_next(p, wk, mb, nb, kb0, kb1)) {
     if (!mbar_wait(&tfull_bar[acc], acc_ph, ab)) break;
     tc_fence_after();
     const int row = mb * unit_rows + row_off + q * 32 + lane;
@@ -554,8 +595,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = warp_id();
   const int lane = lane_id();
-  const int num_units = p.tiles_m * p.tiles_n * p.split_k;
-
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::STAGES; ++i) {
       mbar_init(&full_bar[i], 1);
@@ -586,11 +625,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-        int mb, nb, sk;
-        decode_unit(p, u, mb, nb, sk);
-        const int kb0 = sk * p.kb_per_split;
-        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+      Work wk = work_begin(p, blockIdx.x, gridDim.x);
+      int mb, nb, kb0, kb1;
+      while (ok && work_next(p, wk, mb, nb, kb0, kb1)) {
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[s], ph ^ 1, ab)) { ok = false; break; }
           uint8_t* sA = tiles + s * C::STAGE_BYTES;
@@ -621,11 +658,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_ph = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-        int mb, nb, sk;
-        decode_unit(p, u, mb, nb, sk);
-        const int kb0 = sk * p.kb_per_split;
-        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+      Work wk = work_begin(p, blockIdx.x, gridDim.x);
+      int mb, nb, kb0, kb1;
+      while (ok && work_next(p, wk, mb, nb, kb0, kb1)) {
         if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1, ab)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
@@ -676,7 +711,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
     configured_dev = dev;
   }
   const int units = p.tiles_m * p.tiles_n * p.split_k;
-  const int grid = units < sm_count() ? units : sm_count();
+  const int grid = (p.stream_k || units > sm_count()) ? sm_count() : units;
   launch_kernel(kern, dim3(grid), dim3(kThreads), C::SMEM, stream, 1, ta, tb, tc, tx, p);
   return launch_status();
 }
@@ -734,7 +769,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = warp_id();
   const int lane = lane_id();
   const uint32_t rank = cluster_ctarank();
-  const int num_units = p.tiles_m * p.tiles_n * p.split_k;
   const int unit0 = static_cast<int>(blockIdx.x >> 1), ustride = static_cast<int>(gridDim.x >> 1);
 
   if (threadIdx.x == 0) {
@@ -767,11 +801,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int u = unit0; u < num_units && ok; u += ustride) {
-        int mb, nb, sk;
-        decode_unit(p, u, mb, nb, sk);
-        const int kb0 = sk * p.kb_per_split;
-        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+      Work wk = work_begin(p, unit0, ustride);
+      int mb, nb, kb0, kb1;
+      while (ok && work_next(p, wk, mb, nb, kb0, kb1)) {
         const int arow = mb * BM2 + static_cast<int>(rank) * 128;
         const int bcol = nb * BN2 + static_cast<int>(rank) * 128;
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -808,11 +840,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_ph = 0;
       bool ok = true;
-      for (int u = unit0; u < num_units && ok; u += ustride) {
-        int mb, nb, sk;
-        decode_unit(p, u, mb, nb, sk);
-        const int kb0 = sk * p.kb_per_split;
-        const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+      Work wk = work_begin(p, unit0, ustride);
+      int mb, nb, kb0, kb1;
+      while (ok && work_next(p, wk, mb, nb, kb0, kb1)) {
         if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1, ab)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN2;
@@ -866,7 +896,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   }
   const int units = p.tiles_m * p.tiles_n * p.split_k;
   const int pairs = sm_count() / 2;
-  const int g = units < pairs ? units : pairs;
+  const int g = (p.stream_k || units > pairs) ? pairs : units;
   if (launch_kernel(kern, dim3(2 * g), dim3(kThreads), pair::SMEM, stream, 2, ta, tb, tc, tx, p) != cudaSuccess) {
     cudaGetLastError();
     count_launch();
@@ -1001,6 +1031,32 @@ int gemm_run(const void* A, long long lda, int a_trans, const void* B, long long
         best = eff;
         p.split_k = sk;
       }
+    }
+  }
+  // Stream-K for accumulating GEMMs with few output tiles and a long K (the
+  // weight gradients, K = tokens): equal k-block ranges per worker instead of
+  // whole split-K parts, so no wave is left part-empty.  NL_GEMM_STREAMK=0
+  // turns it off, =1 forces it for every accumulating GEMM.
+  {
+    static int sk_env = -2;
+    if (sk_env == -2) {
+      const char* e = getenv("NL_GEMM_STREAMK");
+      sk_env = e ? atoi(e) : -1;
+    }
+    // measured on the weight-gradient shapes (K = 16384): stream-K wins where
+    // no split-K count fills one wave of workers (512 x 2048: 16 pair tiles,
+    // at best 64 of 74 pairs busy: 39.3 -> 34.4 us) and loses where one does
+    // (512 x 1536: 12 tiles x 6 parts = 72 of 74: 26.9 -> 28.6 us); with more
+    // tiles than workers it spreads each B panel's readers apart in time and
+    // loses its L2 reuse (the LM-head weight gradient: 2.10 -> 2.31 ms)
+    double one_wave = 0.0;
+    for (int sk = 1; sk <= p.num_kb / 8 && static_cast<long long>(tiles) * sk <= wk; ++sk)
+      one_wave = static_cast<double>(tiles) * sk / wk;
+    const bool want = (epi == NL_EPI_ACCUM) &&
+                      (sk_env == 1 || (sk_env != 0 && p.num_kb >= 32 && tiles < wk && one_wave < 0.9));
+    if (want) {
+      p.stream_k = 1;
+      p.split_k = 1;
     }
   }
   p.kb_per_split = (p.num_kb + p.split_k - 1) / p.split_k;

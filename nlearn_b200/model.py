@@ -311,6 +311,7 @@ class AdamW:
             else torch.zeros(3)
         self.t_dev = torch.zeros(1, device=params.device, dtype=torch.int32)  # device step counter
         self.t_dev_value = 0   # what t_dev holds (host view); None when unknown
+        self.zero_grad = False  # clear each gradient element once AdamW has read it
 
     def set_lr(self, lr: float):
         """Stage an explicit learning rate (and this step's bias corrections)
@@ -349,9 +350,10 @@ class AdamW:
 
     def step_range(self, start: int, end: int):
         """AdamW on elements [start, end) of the flat buffers (start, end
-        multiples of 4), on the current stream."""
+        multiples of 4), on the current stream.  With ``zero_grad`` set the
+        kernel clears the gradients it has read."""
         P = self.P
         n = end - start
         check(lib.nl_adamw_step(ptr(P.master[start:]), ptr(P.grad[start:]), ptr(P.exp_avg[start:]),
                                 ptr(P.exp_avg_sq[start:]), ptr(P.shadow[start:]), n, ptr(self.hyper), self.b1,
-                                self.b2, self.eps, self.wd, stream_handle()), "nl_adamw_step")
+                                self.b2, self.eps, self.wd, int(self.zero_grad), stream_handle()), "nl_adamw_step")

@@ -125,7 +125,7 @@ class BucketReducer:
             self.mark = torch.zeros(V, device=dev, dtype=torch.int32)
             self.idx_on = torch.empty(V, device=dev, dtype=torch.int32)
             self.idx_off = torch.empty(V, device=dev, dtype=torch.int32)
-            self.counts = torch.zeros(2, device=dev, dtype=torch.int32)
+            self.counts = torch.zeros(2 + (V + 1023) // 1024, device=dev, dtype=torch.int32)
             self.counts_host = torch.zeros(2, dtype=torch.int32).pin_memory()
             self.counts_event = torch.cuda.Event()
             self.rows_buf = torch.empty(V, D, device=dev, dtype=torch.float32) if self.compact else None
@@ -157,7 +157,7 @@ class BucketReducer:
             check(lib.nl_rows_compact(ptr(self.mark), self.V, ptr(self.idx_on), ptr(self.idx_off), ptr(self.counts),
                                       h), "nl_rows_compact")
             if self.compact:  # the exchange's element count is needed on the host after the backward
-                self.counts_host.copy_(self.counts, non_blocking=True)
+                self.counts_host.copy_(self.counts[:2], non_blocking=True)
                 self.counts_event.record()
             self._adamw_rows(self.idx_off, self.counts[1:], None)
         self._rows_ready = True
@@ -169,7 +169,7 @@ class BucketReducer:
         h = torch.cuda.current_stream().cuda_stream
         check(lib.nl_adamw_rows(ptr(P.master[off:]), None if g is None else ptr(g), ptr(P.exp_avg[off:]),
                                 ptr(P.exp_avg_sq[off:]), ptr(P.shadow[off:]), ptr(idx), ptr(count), self.D, self.V,
-                                ptr(o.hyper), o.b1, o.b2, o.eps, o.wd, h), "nl_adamw_rows")
+                                ptr(o.hyper), o.b1, o.b2, o.eps, o.wd, int(o.zero_grad), h), "nl_adamw_rows")
 
     def ready(self, name: str):
         if not self.active():
@@ -251,6 +251,7 @@ class TrainConfig:
     seed: int = 0
     bucket_mb: int = 64
     fused_lmhead: bool | None = None   # None: NLEARN_FUSED_LMHEAD (model.fused_lmhead_default)
+    keep_grads: bool = False  # False: AdamW clears each gradient after reading it (no zeroing pass per step)
     sparse_embedding_rows: bool = True  # token-table AdamW by rows: untouched rows at the step's start
     compact_embedding_exchange: bool = False  # and all-reduce only the touched rows (host waits for their count)
 
@@ -263,6 +264,9 @@ class Trainer:
         self.P = FlatParams(cfg, self.device, seed=tcfg.seed)   # same init on every rank
         self.model = GPT(cfg, self.P, fused_lmhead=tcfg.fused_lmhead)
         self.opt = AdamW(self.P, weight_decay=tcfg.weight_decay)
+        # with the gradients cleared by the optimizer that consumed them, the
+        # step needs no zeroing pass over the 256 MB gradient buffer
+        self.opt.zero_grad = not tcfg.keep_grads
         # the optimizer runs per bucket, overlapped with the remaining backward,
         # right after that bucket's all-reduce (with one rank: as soon as the
         # bucket's gradients are final); the token table by rows
@@ -286,7 +290,8 @@ class Trainer:
         return tok, tgt
 
     def _step_body(self, tok: torch.Tensor, tgt: torch.Tensor) -> torch.Tensor:
-        self.P.grad.zero_()
+        if not self.opt.zero_grad:
+            self.P.grad.zero_()
         # the schedule (optax warmup_cosine_decay, nlearn/train.py:487-505) is
         # evaluated on the device: no per-step host copy for the host to race
         self.opt.advance_on_device(self.tcfg.peak_lr, self.warmup, self.tcfg.steps, self.tcfg.peak_lr / 10)

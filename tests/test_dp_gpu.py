@@ -35,7 +35,7 @@ def _rank(rank, world, port, out):
     from nlearn_b200.train import Trainer, TrainConfig
     res = {}
     for compact in (False, True):   # whole token-table all-reduce, and touched rows only
-        tr = Trainer(GPTConfig(), TrainConfig(batch=2, seq=128, steps=10, warmup=2, bucket_mb=16,
+        tr = Trainer(GPTConfig(), TrainConfig(batch=2, seq=128, steps=10, warmup=2, bucket_mb=16, keep_grads=True,
                                               compact_embedding_exchange=compact), f"cuda:{rank}", rank, world)
         losses = [tr.train_step(*tr.loader.next()) for _ in range(STEPS)]
         torch.cuda.synchronize()
@@ -62,7 +62,7 @@ def test_dp2_matches_single_gpu_full_batch():
         modes.append((m0, g0))
     runs = []
     for _ in range(2):                # the 1-GPU reference, twice: its own noise floor
-        ref = Trainer(GPTConfig(), TrainConfig(batch=4, seq=128, steps=10, warmup=2), "cuda:0")
+        ref = Trainer(GPTConfig(), TrainConfig(batch=4, seq=128, steps=10, warmup=2, keep_grads=True), "cuda:0")
         m_init = ref.P.master.cpu().numpy()
         a, b = ZipfLoader(2, 128, 50257, 0, 0), ZipfLoader(2, 128, 50257, 0, 1)
         for _ in range(STEPS):

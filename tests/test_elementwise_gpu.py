@@ -72,8 +72,9 @@ def test_adamw_matches_formula(cuda):
     m2 = b1 * m + (1 - b1) * g
     v2 = b2 * v + (1 - b2) * g * g
     p2 = p - lr * ((m2 / (1 - b1 ** t)) / ((v2 / (1 - b2 ** t)).sqrt() + eps) + wd * p)
-    check(lib.nl_adamw_step(ptr(p), ptr(g), ptr(m), ptr(v), ptr(sh), n, ptr(hyper), b1, b2, eps, wd,
+    check(lib.nl_adamw_step(ptr(p), ptr(g), ptr(m), ptr(v), ptr(sh), n, ptr(hyper), b1, b2, eps, wd, 1,
                             stream_handle()), "adamw")
     err = dict(p=(p - p2).abs().max().item(), m=(m - m2).abs().max().item(), v=(v - v2).abs().max().item())
     assert err["p"] < 1e-6 and err["m"] < 1e-6 and err["v"] < 1e-6, err
     assert torch.equal(sh, p.bfloat16())
+    assert int((g != 0).sum()) == 0      # zero_grad: the gradient is cleared for the next step
