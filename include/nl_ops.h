@@ -203,10 +203,11 @@ NL_API int nl_embed_bwd(const int* tok, const float* dx, float* dwte, float* dwp
 NL_API int nl_layernorm_fwd(const void* x, const float* g, const float* b, void* y, float* mean, float* rstd, int M,
                             int D, float eps, cudaStream_t stream);
 /* dres (f32) = (accumulate ? dres : 0) + dLN/dx . dy; dres_bf16 = bf16(dres);
- * dg += sum dy*xhat, db += sum dy. */
+ * dg += sum dy*xhat, db += sum dy; dsum (may be NULL) += column sums of dres
+ * (the bias gradient of the residual branch that dres feeds next). */
 NL_API int nl_layernorm_bwd(const void* dy, const void* x, const float* mean, const float* rstd, const float* g,
-                            float* dres, void* dres_bf16, float* dg, float* db, int M, int D, int accumulate,
-                            cudaStream_t stream);
+                            float* dres, void* dres_bf16, float* dg, float* db, float* dsum, int M, int D,
+                            int accumulate, cudaStream_t stream);
 /* out[N] += column sums of bf16 x[M, N] (N % 8 == 0). */
 NL_API int nl_colsum_bf16(const void* x, float* out, int M, int N, cudaStream_t stream);
 /* AdamW on a flat f32 buffer (optax.adamw semantics); hyper = device

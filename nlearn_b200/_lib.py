@@ -53,7 +53,7 @@ SIGNATURES: dict[str, list] = {
     "nl_embed_fwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
     "nl_embed_bwd": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p],
     "nl_layernorm_fwd": [c_void_p] * 6 + [c_int, c_int, c_float, c_void_p],
-    "nl_layernorm_bwd": [c_void_p] * 9 + [c_int, c_int, c_int, c_void_p],
+    "nl_layernorm_bwd": [c_void_p] * 10 + [c_int, c_int, c_int, c_void_p],
     "nl_colsum_bf16": [c_void_p, c_void_p, c_int, c_int, c_void_p],
     "nl_adamw_step": [c_void_p] * 5 + [c_longlong, c_void_p, c_float, c_float, c_float, c_float, c_int, c_void_p],
     "nl_adamw_schedule": [c_void_p, c_void_p, c_float, c_int, c_int, c_float, c_float, c_float, c_void_p],

@@ -142,19 +142,21 @@ __global__ void layernorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const 
 }
 
 // dx = rstd * (g*dy - mean(g*dy) - xhat * mean(g*dy*xhat));  dres += dx (f32),
-// dres_bf = bf16(dres);  dg += sum_rows dy*xhat, db += sum_rows dy (atomics).
+// dres_bf = bf16(dres);  dg += sum_rows dy*xhat, db += sum_rows dy, and, when
+// dsum is given, dsum += sum_rows dres (the bias gradient of the residual
+// branch that consumes dres: saves a column-sum pass over it) (atomics).
 template <int DV>
 __global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
                                      const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
                                      const float* __restrict__ g, float* dres, __nv_bfloat16* dres_bf, float* dg,
-                                     float* db, int M, int D, int accumulate) {
+                                     float* db, float* dsum, int M, int D, int accumulate) {
   griddep_sync();
   const int lane = threadIdx.x & 31;
-  float adg[DV][8], adb[DV][8];
+  float adg[DV][8], adb[DV][8], ads[DV][8];
 #pragma unroll
   for (int j = 0; j < DV; ++j)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) adg[j][i] = adb[j][i] = 0.f;
+    for (int i = 0; i < 8; ++i) adg[j][i] = adb[j][i] = ads[j][i] = 0.f;
   float gg[DV][8];
 #pragma unroll
   for (int j = 0; j < DV; ++j) {
@@ -195,7 +197,10 @@ __global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const
       const float4 r1 = accumulate ? rr[2 * (lane + 32 * j) + 1] : make_float4(0, 0, 0, 0);
       const float prev[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = prev[i] + rstd * (gd[j][i] - c1 - xh[j][i] * c2);
+      for (int i = 0; i < 8; ++i) {
+        o[i] = prev[i] + rstd * (gd[j][i] - c1 - xh[j][i] * c2);
+        ads[j][i] += o[i];
+      }
       rr[2 * (lane + 32 * j)] = make_float4(o[0], o[1], o[2], o[3]);
       rr[2 * (lane + 32 * j) + 1] = make_float4(o[4], o[5], o[6], o[7]);
       rb[lane + 32 * j] = pack8(o);
@@ -206,18 +211,20 @@ __global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const
   // atomics do not serialise on the D hot addresses).
   __shared__ float red[8][DV * 256];
   const int w = threadIdx.x >> 5;
-#pragma unroll
-  for (int which = 0; which < 2; ++which) {
+  const int nsums = dsum ? 3 : 2;
+  for (int which = 0; which < nsums; ++which) {
 #pragma unroll
     for (int j = 0; j < DV; ++j)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) red[w][(lane + 32 * j) * 8 + i] = which ? adb[j][i] : adg[j][i];
+      for (int i = 0; i < 8; ++i)
+        red[w][(lane + 32 * j) * 8 + i] = which == 2 ? ads[j][i] : which ? adb[j][i] : adg[j][i];
     __syncthreads();
+    float* dst = which == 2 ? dsum : which ? db : dg;
     for (int c = threadIdx.x; c < D; c += blockDim.x) {
       float t = 0.f;
 #pragma unroll
       for (int k = 0; k < 8; ++k) t += red[k][c];
-      atomicAdd((which ? db : dg) + c, t);
+      atomicAdd(dst + c, t);
     }
     __syncthreads();
   }
@@ -542,8 +549,8 @@ extern "C" int nl_layernorm_fwd(const void* x, const float* g, const float* b, v
 }
 
 extern "C" int nl_layernorm_bwd(const void* dy, const void* x, const float* mean, const float* rstd, const float* g,
-                                float* dres, void* dres_bf16, float* dg, float* db, int M, int D, int accumulate,
-                                cudaStream_t stream) {
+                                float* dres, void* dres_bf16, float* dg, float* db, float* dsum, int M, int D,
+                                int accumulate, cudaStream_t stream) {
   if (M <= 0 || D % 256) return NL_ERR_SHAPE;
   const auto* dyi = static_cast<const __nv_bfloat16*>(dy);
   const auto* xi = static_cast<const __nv_bfloat16*>(x);
@@ -552,13 +559,13 @@ extern "C" int nl_layernorm_bwd(const void* dy, const void* x, const float* mean
   if (grid > 2 * sm_count()) grid = 2 * sm_count();  // few blocks: cheap gamma/beta atomics
   switch (D / 256) {
     case 1:
-      launch_kernel(ew::layernorm_bwd_kernel<1>, dim3(grid), dim3(256), 0, stream, 1, dyi, xi, mean, rstd, g, dres, rb, dg, db, M, D, accumulate);
+      launch_kernel(ew::layernorm_bwd_kernel<1>, dim3(grid), dim3(256), 0, stream, 1, dyi, xi, mean, rstd, g, dres, rb, dg, db, dsum, M, D, accumulate);
       break;
     case 2:
-      launch_kernel(ew::layernorm_bwd_kernel<2>, dim3(grid), dim3(256), 0, stream, 1, dyi, xi, mean, rstd, g, dres, rb, dg, db, M, D, accumulate);
+      launch_kernel(ew::layernorm_bwd_kernel<2>, dim3(grid), dim3(256), 0, stream, 1, dyi, xi, mean, rstd, g, dres, rb, dg, db, dsum, M, D, accumulate);
       break;
     case 4:
-      launch_kernel(ew::layernorm_bwd_kernel<4>, dim3(grid), dim3(256), 0, stream, 1, dyi, xi, mean, rstd, g, dres, rb, dg, db, M, D, accumulate);
+      launch_kernel(ew::layernorm_bwd_kernel<4>, dim3(grid), dim3(256), 0, stream, 1, dyi, xi, mean, rstd, g, dres, rb, dg, db, dsum, M, D, accumulate);
       break;
     default: return NL_ERR_SHAPE;
   }

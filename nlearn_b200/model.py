@@ -156,9 +156,12 @@ def _ln_fwd(x, g, b, eps, M, D):
     return y, mean, rstd
 
 
-def _ln_bwd(dy, x, mean, rstd, g, dres, dres_bf, dg, db, M, D, accumulate):
+def _ln_bwd(dy, x, mean, rstd, g, dres, dres_bf, dg, db, M, D, accumulate, dsum=None):
+    """LayerNorm backward into the residual gradient; ``dsum`` (optional)
+    accumulates the column sums of the new residual gradient, i.e. the bias
+    gradient of the FFN output projection that consumes it next."""
     check(lib.nl_layernorm_bwd(ptr(dy), ptr(x), ptr(mean), ptr(rstd), ptr(g), ptr(dres), ptr(dres_bf), ptr(dg),
-                               ptr(db), M, D, int(accumulate), stream_handle()), "nl_layernorm_bwd")
+                               ptr(db), ptr(dsum), M, D, int(accumulate), stream_handle()), "nl_layernorm_bwd")
 
 
 class GPT:
@@ -243,8 +246,9 @@ class GPT:
             notify("head.w")
         dres = torch.empty(M, D, device=dev, dtype=torch.float32)
         dres_bf = torch.empty(M, D, device=dev, dtype=torch.bfloat16)
+        last = f"blocks.{cfg.n_layers - 1}."
         _ln_bwd(dhf_bf, saved["xf"], saved["mf"], saved["rf"], P.f("lnf.g"), dres, dres_bf, P.g("lnf.g"),
-                P.g("lnf.b"), M, D, accumulate=False)
+                P.g("lnf.b"), M, D, accumulate=False, dsum=P.g(last + "b2"))
         notify("lnf.g"); notify("lnf.b")
         qs = (3 * D, 64, S * 3 * D)
         os_ = (D, 64, S * D)
@@ -252,8 +256,8 @@ class GPT:
             pre = f"blocks.{layer}."
             sv = saved["layers"][layer]
             # x3 = x2 + u @ W2 + b2
+            # (b2's gradient, the column sums of dres, came with the LayerNorm backward that made dres)
             gemm_ex(sv["u"], dres_bf, a_trans=True, out=P.g(pre + "w2"), epilogue=_lib.EPI_ACCUM)
-            check(lib.nl_colsum_bf16(ptr(dres_bf), ptr(P.g(pre + "b2")), M, D, stream_handle()), "colsum")
             da = gemm_ex(dres_bf, P.p(pre + "w2"), b_trans=True, out_dtype=torch.bfloat16,
                          epilogue=_lib.EPI_DGELU, aux=sv["a"])           # d(pre-activation)
             notify(pre + "w2"); notify(pre + "b2")   # (after the last read of W2)
@@ -280,7 +284,8 @@ class GPT:
             dh1 = gemm_ex(dqkv, P.p(pre + "wqkv"), b_trans=True, out_dtype=torch.bfloat16)
             notify(pre + "wqkv")
             _ln_bwd(dh1, sv["x"], sv["m1"], sv["r1"], P.f(pre + "ln1.g"), dres, dres_bf, P.g(pre + "ln1.g"),
-                    P.g(pre + "ln1.b"), M, D, accumulate=True)
+                    P.g(pre + "ln1.b"), M, D, accumulate=True,
+                    dsum=P.g(f"blocks.{layer - 1}.b2") if layer > 0 else None)
             notify(pre + "ln1.g"); notify(pre + "ln1.b")
         check(lib.nl_embed_bwd(ptr(saved["tok"]), ptr(dres), ptr(P.g("wte")), ptr(P.g("wpe")), M, S, D,
                                stream_handle()), "nl_embed_bwd")

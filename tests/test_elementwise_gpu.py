@@ -32,8 +32,10 @@ def test_layernorm_fwd_bwd(cuda, M, D):
     dres_bf = torch.empty(M, D, device=cuda, dtype=torch.bfloat16)
     dg = torch.zeros(D, device=cuda)
     db = torch.zeros(D, device=cuda)
+    ds = torch.full((D,), 0.5, device=cuda)
     check(lib.nl_layernorm_bwd(ptr(dy), ptr(x), ptr(mean), ptr(rstd), ptr(g), ptr(dres), ptr(dres_bf), ptr(dg),
-                               ptr(db), M, D, 1, stream_handle()), "ln bwd")
+                               ptr(db), ptr(ds), M, D, 1, stream_handle()), "ln bwd")
+    assert rel(ds - 0.5, dres.sum(0)) < 1e-4        # column sums of the new residual gradient, accumulated
     assert rel(dres - 1, xr.grad) < 1e-3
     assert rel(dres_bf, dres) < 1e-2
     assert rel(dg, gr.grad) < 1e-3 and rel(db, br.grad) < 1e-3
