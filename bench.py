@@ -16,9 +16,10 @@ Reported (one JSON line from rank 0):
                  the steps are replays of one captured CUDA graph of the whole
                  step (Trainer.capture_step / step_graphed); with N > 1 ranks
                  they are eager launches.  The eager figure is also reported.
-  e2e            same metric through the public API (Trainer.step_graphed, or
-                 step_on_device for N > 1: host token arrays in pinned memory
-                 -> H2D copy -> step -> loss read back, every step)
+  e2e            same metric through the public API (Trainer.train_step_async:
+                 host token arrays in pinned memory -> H2D copy -> step (graph
+                 replay at one rank, eager with N > 1) -> D2H copy of the loss,
+                 every step; the host reads each loss one step late)
   roofline       the dominant launch family of the step: the 16 weight-gradient
                  GEMMs of the four blocks (gemm_pair_kernel<1,1>, dW += X^T dY
                  at K = 16384), timed live with CUDA events on the launching
@@ -630,14 +631,17 @@ def main():
     f0 = torch.cuda.Event(enable_timing=True)
     f1 = torch.cuda.Event(enable_timing=True)
     f0.record()
+    if not graphed:
+        tr._graph = None
+    lv = None
     for x, y in pinned:
-        if graphed:
-            lv = float(tr.step_graphed(x, y))   # H2D of the batch into the graph's inputs, D2H of the loss
-        else:
-            tok = x.to(dev, non_blocking=True)
-            tgt = y.to(dev, non_blocking=True)
-            lv = float(tr.step_on_device(tok, tgt))   # D2H read of the loss
+        # H2D of the batch, the step, D2H of its loss into pinned memory; the
+        # host reads the previous step's loss (so it never waits on the step
+        # it has just queued)
+        prev = tr.train_step_async(x, y)
+        lv = prev if prev is not None else lv
     f1.record()
+    lv = tr.flush_loss()                       # the last step's loss, read inside the timed region
     barrier()
     t2 = torch.tensor([f0.elapsed_time(f1)], device=dev)
     if world > 1:

@@ -367,6 +367,41 @@ class Trainer:
         tok, tgt = self.device_batch(inputs, targets)
         return float(self.step_on_device(tok, tgt))
 
+    def train_step_async(self, inputs: torch.Tensor, targets: torch.Tensor):
+        """Host batch in (pinned CPU int32 tensors), host loss out one step
+        late: the step is launched (the replayed CUDA graph at one rank when
+        captured, else eager), its loss is copied into a pinned host slot, and
+        the PREVIOUS step's loss is returned (None on the first call), so the
+        host never waits for the step it has just queued.  ``flush_loss()``
+        returns the last one."""
+        if getattr(self, "_graph", None) is not None:
+            loss = self.step_graphed(inputs, targets)
+        else:
+            loss = self.step_on_device(inputs.to(self.device, non_blocking=True),
+                                       targets.to(self.device, non_blocking=True))
+        if not hasattr(self, "_loss_slots"):
+            self._loss_slots = [torch.zeros(1, dtype=torch.float32).pin_memory() for _ in range(2)]
+            self._loss_events = [torch.cuda.Event(), torch.cuda.Event()]
+            self._loss_k = 0
+            self._loss_pending = None
+        k = self._loss_k
+        self._loss_slots[k].copy_(loss.reshape(1), non_blocking=True)
+        self._loss_events[k].record()
+        prev, self._loss_pending, self._loss_k = self._loss_pending, k, k ^ 1
+        if prev is None:
+            return None
+        self._loss_events[prev].synchronize()
+        return float(self._loss_slots[prev][0])
+
+    def flush_loss(self):
+        """The loss of the last train_step_async call (waits for that step)."""
+        k = getattr(self, "_loss_pending", None)
+        if k is None:
+            return None
+        self._loss_events[k].synchronize()
+        self._loss_pending = None
+        return float(self._loss_slots[k][0])
+
     # ------------------------------------------------------------- checkpoint
     def save(self, path: str):
         if self.rank != 0:

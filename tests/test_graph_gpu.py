@@ -62,3 +62,23 @@ def test_graph_replay_matches_eager(cuda):
     l1 = float(a.step_on_device(*dev[1]))
     l2 = float(b.step_graphed(*dev[1]))
     assert abs(l1 - l2) < 1e-3
+
+
+def test_train_step_async_returns_each_loss_one_step_late(cuda):
+    """train_step_async (pinned host batches in, the previous step's loss out)
+    gives the same loss sequence as the synchronous train_step."""
+    import numpy as np
+    from nlearn_b200.model import GPTConfig
+    from nlearn_b200.train import Trainer, TrainConfig
+    cfg = GPTConfig()
+    tc = TrainConfig(batch=2, seq=128, steps=20, warmup=2)
+    a, b = Trainer(cfg, tc, cuda), Trainer(cfg, tc, cuda)
+    batches = [a.loader.next() for _ in range(4)]
+    sync = [a.train_step(x, y) for x, y in batches]
+    got = []
+    for x, y in batches:
+        r = b.train_step_async(torch.from_numpy(x).pin_memory(), torch.from_numpy(y).pin_memory())
+        if r is not None:
+            got.append(r)
+    got.append(b.flush_loss())
+    assert np.allclose(got, sync, rtol=0, atol=2e-3), (got, sync)
