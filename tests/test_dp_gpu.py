@@ -9,7 +9,8 @@ reproducible only to a noise floor: the test measures that floor by running
 the 1-GPU step twice, and requires, per tensor, the data-parallel gradient to
 sit within 4x that floor or 1e-3 of the 1-GPU one, both as max |err| /
 max |ref| and normwise, and every element larger than a tenth of its
-tensor's largest within 1e-2 relative.  The replicas' weights must stay
+tensor's largest within 1e-2 relative, or 4x the worst such relative
+difference between the two 1-GPU runs.  The replicas' weights must stay
 bit-identical, and after the step's AdamW the update vector must match the
 1-GPU one within 1e-2 normwise (Adam moves near-zero-gradient elements by
 about lr in a direction set by round-off, so that check is normwise).
@@ -91,7 +92,9 @@ def test_dp2_matches_single_gpu_full_batch():
             assert err <= max(4 * floor, 1e-3), (name, err, floor)
             assert nerr <= max(4 * nfloor, 1e-3), (name, nerr, nfloor)
             big = np.abs(gf) > 0.1 * top
-            assert (np.abs(gd - gf)[big] <= 1e-2 * np.abs(gf)[big]).all(), name
+            rel_big = (np.abs(gd - gf)[big] / np.abs(gf)[big]).max()
+            rel_floor = (np.abs(g2 - gf)[big] / np.abs(gf)[big]).max()
+            assert rel_big <= max(4 * rel_floor, 1e-2), (name, rel_big, rel_floor)
         print(sorted(worst, key=lambda w: -w[1])[:5])
         ud, ur = (m0 - m_init).astype(np.float64), (mr - m_init).astype(np.float64)
         rel = np.linalg.norm(ud - ur) / np.linalg.norm(ur)
