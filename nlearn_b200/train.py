@@ -249,7 +249,11 @@ class TrainConfig:
     warmup: int = 200          # the BASELINE warmup; capped at steps // 5 as train.py:488
     weight_decay: float = 0.1
     seed: int = 0
-    bucket_mb: int = 64
+    # layer-sized buckets (a block's parameters are 12.6 MB in f32): each
+    # block's exchange starts as soon as that block's backward is done, so only
+    # the first block and the token table are left for the step's tail (with
+    # 64 MB buckets the four blocks shared one bucket, launched at the end)
+    bucket_mb: int = 16
     fused_lmhead: bool | None = None   # None: NLEARN_FUSED_LMHEAD (model.fused_lmhead_default)
     # False: AdamW clears each gradient after reading it and the step skips its
     # zeroing pass; measured 0.4 ms/step slower on B200 (the clearing writes
@@ -274,9 +278,7 @@ class Trainer:
         # right after that bucket's all-reduce (with one rank: as soon as the
         # bucket's gradients are final); the token table by rows
         overlap = self.device.type == "cuda" or world > 1
-        # one rank: no collective to amortise, so layer-sized buckets hide more of the optimizer
-        bucket_mb = tcfg.bucket_mb if world > 1 else min(tcfg.bucket_mb, 16)
-        self.reducer = BucketReducer(self.P, bucket_mb << 20, group, optimizer=self.opt if overlap else None,
+        self.reducer = BucketReducer(self.P, tcfg.bucket_mb << 20, group, optimizer=self.opt if overlap else None,
                                      sparse_rows=tcfg.sparse_embedding_rows and self.device.type == "cuda",
                                      compact_exchange=tcfg.compact_embedding_exchange)
         self.loader = ZipfLoader(tcfg.batch, tcfg.seq, cfg.vocab, tcfg.seed, rank)
