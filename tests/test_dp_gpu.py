@@ -13,8 +13,9 @@ tensor's largest within 1e-2 relative, or 4x the worst such relative
 difference between the two 1-GPU runs.  The replicas' weights must stay
 bit-identical, and after the step's AdamW (no warmup, so the first step
 moves the weights) the update vector must match the
-1-GPU one within 1e-2 normwise (Adam moves near-zero-gradient elements by
-about lr in a direction set by round-off, so that check is normwise).
+1-GPU one within 1e-2 normwise or 4x the two 1-GPU runs' own difference
+(Adam's first step is about lr * sign(g), so near-zero gradients move either
+way under round-off).
 Skipped when fewer than 2 GPUs are visible."""
 import os
 
@@ -74,7 +75,7 @@ def test_dp2_matches_single_gpu_full_batch():
         runs.append((ref.P.master.cpu().numpy(), ref.P.grad.cpu().numpy()))
         offsets, specs = ref.P.offsets, ref.P.specs
         del ref
-    (mr, gr), (_, gr2) = runs
+    (mr, gr), (mr2, gr2) = runs
     for m0, g0 in modes:
         worst = []
         for name, _, _ in specs:
@@ -97,6 +98,7 @@ def test_dp2_matches_single_gpu_full_batch():
             rel_floor = (np.abs(g2 - gf)[big] / np.abs(gf)[big]).max()
             assert rel_big <= max(4 * rel_floor, 1e-2), (name, rel_big, rel_floor)
         print(sorted(worst, key=lambda w: -w[1])[:5])
-        ud, ur = (m0 - m_init).astype(np.float64), (mr - m_init).astype(np.float64)
+        ud, ur, ur2 = ((x - m_init).astype(np.float64) for x in (m0, mr, mr2))
         rel = np.linalg.norm(ud - ur) / np.linalg.norm(ur)
-        assert rel < 1e-2, rel
+        rel_floor = np.linalg.norm(ur2 - ur) / np.linalg.norm(ur)
+        assert rel <= max(4 * rel_floor, 1e-2), (rel, rel_floor)
