@@ -271,6 +271,16 @@ NL_API int nl_lce_bwd(const void* X, int ldx, const void* W, int ldw, const int*
                       const float* gscale, float grad_mul, float* dX, float* dW, int lddw, int dw_accumulate,
                       void* workspace, size_t ws_bytes, int chunk, int M, int D, int V, cudaStream_t stream);
 
+/* nl_lce_bwd with the dX output chosen by the caller: dx_accumulate = 0
+ * stores dX (no zeroing needed) instead of adding to it, and dx_dtype may then
+ * be NL_BF16 when one chunk covers the vocabulary (chunk >= V), which hands the
+ * next layer its bf16 gradient directly.  Same reference interface as
+ * nl_lce_bwd (nlearn/kernels/cross_entropy.py:131-170). */
+NL_API int nl_lce_bwd_ex(const void* X, int ldx, const void* W, int ldw, const int* targets, const float* lse,
+                         const float* gscale, float grad_mul, void* dX, int dx_dtype, int dx_accumulate, float* dW,
+                         int lddw, int dw_accumulate, void* workspace, size_t ws_bytes, int chunk, int M, int D,
+                         int V, cudaStream_t stream);
+
 /* ---------------------------------------------------------------- decode (inference)
  * Replace the reference's generate loop (nlearn/model.py:417-465: full
  * recompute per token, jax.random.categorical sampling) with KV-cache decode

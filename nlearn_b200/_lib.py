@@ -76,6 +76,8 @@ SIGNATURES: dict[str, list] = {
     "nl_lce_workspace_bytes": [c_int, c_int, c_int],
     "nl_lce_fwd": [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t,
                    c_int, c_int, c_int, c_void_p],
+    "nl_lce_bwd_ex": [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_int, c_int,
+                      c_void_p, c_int, c_int, c_void_p, ctypes.c_size_t, c_int, c_int, c_int, c_int, c_void_p],
     "nl_lce_bwd": [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
                    c_int, c_int, c_void_p, ctypes.c_size_t, c_int, c_int, c_int, c_int, c_void_p],
 }

@@ -126,11 +126,17 @@ extern "C" int nl_lce_fwd(const void* X, int ldx, const void* W, int ldw, const 
   return launch_status();
 }
 
-extern "C" int nl_lce_bwd(const void* X, int ldx, const void* W, int ldw, const int* targets, const float* lse,
-                          const float* gscale, float grad_mul, float* dX, float* dW, int lddw, int dw_accumulate,
-                          void* workspace, size_t ws_bytes, int chunk, int M, int D, int V, cudaStream_t stream) {
+namespace {
+// dX: dx_accumulate -> f32 dX += dl W^T over every chunk; otherwise the first
+// chunk stores (in dx_dtype) and later chunks accumulate (f32 only).
+int lce_bwd_impl(const void* X, int ldx, const void* W, int ldw, const int* targets, const float* lse,
+                 const float* gscale, float grad_mul, void* dX, int dx_dtype, int dx_accumulate, float* dW, int lddw,
+                 int dw_accumulate, void* workspace, size_t ws_bytes, int chunk, int M, int D, int V,
+                 cudaStream_t stream) {
   if (M <= 0 || D <= 0 || V <= 0 || ldx < D || ldw < V || lddw < V) return NL_ERR_SHAPE;
   if (chunk <= 0 || (chunk & 63)) return NL_ERR_SHAPE;
+  if (dx_dtype != NL_F32 && dx_dtype != NL_BF16) return NL_ERR_DTYPE;
+  if (dx_dtype == NL_BF16 && (dx_accumulate || chunk < V)) return NL_ERR_DTYPE;
   const lce::Layout L = lce::layout(M, V, chunk);
   if (!workspace || ws_bytes < L.total) return NL_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(workspace) & 255) return NL_ERR_ALIGN;
@@ -149,8 +155,9 @@ extern "C" int nl_lce_bwd(const void* X, int ldx, const void* W, int ldw, const 
                       nullptr, nullptr, stream, &ex);
     if (st) return st;
     if (dX) {
-      st = gemm_run(dl, chunk, 0, Wb + cs, ldw, 1, dX, D, NL_F32, M, D, vc, 1.f, NL_EPI_ACCUM, nullptr, nullptr,
-                    nullptr, stream, nullptr);
+      const bool store = !dx_accumulate && cs == 0;
+      st = gemm_run(dl, chunk, 0, Wb + cs, ldw, 1, dX, D, store ? dx_dtype : NL_F32, M, D, vc, 1.f,
+                    store ? NL_EPI_STORE : NL_EPI_ACCUM, nullptr, nullptr, nullptr, stream, nullptr);
       if (st) return st;
     }
     if (dW) {
@@ -160,4 +167,20 @@ extern "C" int nl_lce_bwd(const void* X, int ldx, const void* W, int ldw, const 
     }
   }
   return NL_OK;
+}
+}  // namespace
+
+extern "C" int nl_lce_bwd(const void* X, int ldx, const void* W, int ldw, const int* targets, const float* lse,
+                          const float* gscale, float grad_mul, float* dX, float* dW, int lddw, int dw_accumulate,
+                          void* workspace, size_t ws_bytes, int chunk, int M, int D, int V, cudaStream_t stream) {
+  return lce_bwd_impl(X, ldx, W, ldw, targets, lse, gscale, grad_mul, dX, NL_F32, 1, dW, lddw, dw_accumulate,
+                      workspace, ws_bytes, chunk, M, D, V, stream);
+}
+
+extern "C" int nl_lce_bwd_ex(const void* X, int ldx, const void* W, int ldw, const int* targets, const float* lse,
+                             const float* gscale, float grad_mul, void* dX, int dx_dtype, int dx_accumulate,
+                             float* dW, int lddw, int dw_accumulate, void* workspace, size_t ws_bytes, int chunk,
+                             int M, int D, int V, cudaStream_t stream) {
+  return lce_bwd_impl(X, ldx, W, ldw, targets, lse, gscale, grad_mul, dX, dx_dtype, dx_accumulate, dW, lddw,
+                      dw_accumulate, workspace, ws_bytes, chunk, M, D, V, stream);
 }

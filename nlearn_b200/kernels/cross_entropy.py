@@ -164,6 +164,26 @@ def lce_bwd_raw(Xb, Wb, t, lse, g=None, dX=None, dW=None, dw_accumulate=False, c
     return dX, dW
 
 
+def lce_bwd_bf16_dx(Xb, Wb, t, lse, dW, dw_accumulate=True):
+    """-> dX bf16 [M, D] written (not accumulated) by the LM head's dX GEMM
+    (nl_lce_bwd_ex), with dW as lce_bwd_raw: no zeroed f32 dX and no cast
+    pass.  Needs one vocabulary chunk (the default at the step's sizes);
+    otherwise it accumulates in f32 and casts."""
+    M, D = Xb.shape
+    V = Wb.shape[1]
+    chunk = _balanced_chunk(V, _default_chunk(M))
+    if chunk < V:
+        dX, _ = lce_bwd_raw(Xb, Wb, t, lse, dW=dW, dw_accumulate=dw_accumulate, chunk=chunk)
+        return dX.to(torch.bfloat16)
+    dX = torch.empty(M, D, device=Xb.device, dtype=torch.bfloat16)
+    nbytes = lib.nl_lce_workspace_bytes(M, V, chunk)
+    ws = torch.empty(nbytes, device=Xb.device, dtype=torch.uint8)
+    check(lib.nl_lce_bwd_ex(ptr(Xb), Xb.stride(0), ptr(Wb), Wb.stride(0), ptr(t), ptr(lse), None, 1.0 / M, ptr(dX),
+                            BF16, 0, ptr(dW), dW.stride(0), int(dw_accumulate), ptr(ws), nbytes, chunk, M, D, V,
+                            stream_handle()), "nl_lce_bwd_ex")
+    return dX
+
+
 class _LCE(torch.autograd.Function):
     @staticmethod
     def forward(ctx, X, W, targets):
@@ -190,4 +210,4 @@ def linear_cross_entropy(X: torch.Tensor, W: torch.Tensor, targets: torch.Tensor
 
 
 __all__ = ["cross_entropy", "linear_cross_entropy", "_ce_fwd_raw", "_ce_bwd_raw", "ce_fwd_bwd", "lce_fwd_raw",
-           "lce_bwd_raw"]
+           "lce_bwd_raw", "lce_bwd_bf16_dx"]

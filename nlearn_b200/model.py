@@ -41,7 +41,7 @@ import torch
 from . import _lib
 from ._lib import check, lib, ptr, stream_handle
 from .kernels.gemm import gemm_ex
-from .kernels.cross_entropy import ce_fwd_bwd, lce_bwd_raw, lce_fwd_raw
+from .kernels.cross_entropy import ce_fwd_bwd, lce_bwd_bf16_dx, lce_fwd_raw
 
 
 def fused_lmhead_default() -> bool:
@@ -233,12 +233,9 @@ class GPT:
         notify = on_grad_ready or (lambda name: None)
         t = saved["targets"].reshape(-1)
         if self.fused_lmhead:
-            # LM head + CE: dhf (f32) and d head.w accumulated in place
-            dhf = torch.zeros(M, D, device=dev, dtype=torch.float32)
-            lce_bwd_raw(saved["hf"], P.p("head.w")[:, :V], t, saved["lse"], dX=dhf,
-                        dW=P.g("head.w")[:, :V], dw_accumulate=True)
+            # LM head + CE: dhf written in bf16 by the dX GEMM, d head.w accumulated in place
+            dhf_bf = lce_bwd_bf16_dx(saved["hf"], P.p("head.w")[:, :V], t, saved["lse"], dW=P.g("head.w")[:, :V])
             notify("head.w")
-            dhf_bf = dhf.to(torch.bfloat16)
         else:
             dl = saved["dlogits"]                      # bf16 [M, V], already / M
             gemm_ex(saved["hf"], dl, a_trans=True, out=P.g("head.w")[:, :V], epilogue=_lib.EPI_ACCUM)

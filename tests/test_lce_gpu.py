@@ -83,3 +83,24 @@ def test_full_size_properties(cuda):
     logits = X.float() @ W.float()
     ref = torch.nn.functional.cross_entropy(logits, t.long()).item()
     assert abs(loss - ref) < 1e-3
+
+
+def test_bwd_ex_writes_bf16_dx(cuda):
+    """nl_lce_bwd_ex storing a bf16 dX (no zeroed f32 buffer, no cast) gives
+    the accumulating nl_lce_bwd's dX rounded to bf16, and the same dW."""
+    torch.manual_seed(4)
+    M, D, V = 2048, 512, 50257
+    Vp = (V + 63) // 64 * 64
+    X = torch.randn(M, D, device=cuda).bfloat16()
+    W = (torch.randn(D, Vp, device=cuda) * 0.02).bfloat16()[:, :V]
+    t = torch.randint(0, V, (M,), device=cuda, dtype=torch.int32)
+    loss, lse = CE.lce_fwd_raw(X, W, t)
+    dW1 = torch.zeros(D, Vp, device=cuda)[:, :V]
+    dX1, _ = CE.lce_bwd_raw(X, W, t, lse, dW=dW1, dw_accumulate=True)
+    dW2 = torch.zeros(D, Vp, device=cuda)[:, :V]
+    dX2 = CE.lce_bwd_bf16_dx(X, W, t, lse, dW=dW2)
+    torch.cuda.synchronize()
+    assert dX2.dtype == torch.bfloat16
+    assert nrel(dX2.float().cpu().numpy(), dX1.cpu().numpy()) < 1e-2
+    assert nrel(dW2.cpu().numpy(), dW1.cpu().numpy()) < 1e-5
+    assert _lib.device_error() == 0
