@@ -509,6 +509,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--compact-exchange", action="store_true",
+                    help="all-reduce only the token-table rows the batch touched (N > 1)")
     ap.add_argument("--no-long", action="store_true", help="skip the seq-4096 long-context measurement")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of CUDA-graph replay")
     ap.add_argument("--no-extras", action="store_true",
@@ -529,7 +531,8 @@ def main():
     dev = torch.device(f"cuda:{local}")
     torch.cuda.set_device(dev)
     cfg = GPTConfig()
-    tr = Trainer(cfg, TrainConfig(batch=BATCH, seq=SEQ, steps=1000, peak_lr=1e-3, warmup=200), dev, rank, world)
+    tr = Trainer(cfg, TrainConfig(batch=BATCH, seq=SEQ, steps=1000, peak_lr=1e-3, warmup=200,
+                                  compact_embedding_exchange=args.compact_exchange), dev, rank, world)
 
     # device-resident batches for the timed region
     nb = args.warmup + args.steps
