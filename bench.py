@@ -509,6 +509,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sharded-optimizer", action="store_true",
+                    help="N > 1: reduce-scatter, AdamW on this rank's shard, all-gather the weights")
     ap.add_argument("--compact-exchange", action="store_true",
                     help="all-reduce only the token-table rows the batch touched (N > 1)")
     ap.add_argument("--no-long", action="store_true", help="skip the seq-4096 long-context measurement")
@@ -532,7 +534,8 @@ def main():
     torch.cuda.set_device(dev)
     cfg = GPTConfig()
     tr = Trainer(cfg, TrainConfig(batch=BATCH, seq=SEQ, steps=1000, peak_lr=1e-3, warmup=200,
-                                  compact_embedding_exchange=args.compact_exchange), dev, rank, world)
+                                  compact_embedding_exchange=args.compact_exchange,
+                                  sharded_optimizer=args.sharded_optimizer), dev, rank, world)
 
     # device-resident batches for the timed region
     nb = args.warmup + args.steps

@@ -90,9 +90,15 @@ def _align(n: int, a: int = 64) -> int:
     return (n + a - 1) // a * a
 
 
+# Every parameter starts on a 512-element (2 KB) boundary: then any run of
+# whole parameters, padded to the next boundary, splits into 2, 4 or 8 equal
+# 256-byte aligned shards (the sharded optimizer's reduce-scatter / all-gather).
+PARAM_ALIGN = 512
+
+
 class FlatParams:
     """All parameters in one f32 master buffer (+ bf16 compute copy, f32 grads,
-    AdamW moments), each parameter a view at a 256-byte aligned offset."""
+    AdamW moments), each parameter a view at a 2 KB aligned offset."""
 
     def __init__(self, cfg: GPTConfig, device, seed: int = 0):
         self.cfg = cfg
@@ -101,7 +107,7 @@ class FlatParams:
         off = 0
         for name, shape, _ in self.specs:
             self.offsets[name] = (off, shape)
-            off = _align(off + math.prod(shape))
+            off = _align(off + math.prod(shape), PARAM_ALIGN)
         self.numel = off
         self.device = torch.device(device)
         self.master = torch.zeros(self.numel, device=self.device, dtype=torch.float32)

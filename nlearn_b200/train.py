@@ -80,7 +80,7 @@ class BucketReducer:
     AdamW."""
 
     def __init__(self, params: FlatParams, bucket_bytes: int = 64 << 20, group=None, optimizer=None,
-                 sparse_rows: bool | None = None, compact_exchange: bool = False):
+                 sparse_rows: bool | None = None, compact_exchange: bool = False, sharded: bool = False):
         self.P = params
         self.optimizer = optimizer  # if set, each bucket's AdamW runs right after its all-reduce
         self.group = group
@@ -94,6 +94,14 @@ class BucketReducer:
         # gradient is all-reduced (zero on untouched rows) and only the AdamW
         # is split by rows
         self.compact = self.sparse and compact_exchange and self.world > 1
+        # ZeRO-1 style: reduce-scatter each bucket, AdamW on this rank's shard,
+        # all-gather the updated master weights (the same NVLink bytes as the
+        # all-reduce, 1/world of the optimizer work); bucket ranges are padded
+        # to the parameters' 2 KB alignment so they split evenly
+        from .model import PARAM_ALIGN
+        self.sharded = (sharded and self.world > 1 and optimizer is not None and cuda
+                        and (PARAM_ALIGN // 64) % self.world == 0)
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         cap = max(1, bucket_bytes // 4)
         self.buckets = []  # (start, end, {names})
         cur_names, start = set(), None
@@ -113,6 +121,9 @@ class BucketReducer:
                 cur_names, start = set(), None
         if cur_names:
             self.buckets.append((start, end, cur_names))
+        if self.sharded:   # extend each bucket over the padding up to the next parameter
+            self.buckets = [(st, min(-(-en // PARAM_ALIGN) * PARAM_ALIGN, params.numel), ns)
+                            for st, en, ns in self.buckets]
         self.owner = {n: i for i, (_, _, ns) in enumerate(self.buckets) for n in ns}
         self.stream = torch.cuda.Stream(device=params.device) if cuda else None
         self._pending = None
@@ -195,11 +206,46 @@ class BucketReducer:
         if self.sparse and names == {"wte"} and self._rows_ready:
             self._process_rows()
             return
+        if self.sharded:
+            self._process_sharded(start, end)
+            return
         buf = self.P.grad[start:end]
         if self.world > 1:
             self._allreduce(buf)
         if self.optimizer is not None:
             self.optimizer.step_range(start, end)
+
+    def _shard(self, start: int, end: int):
+        c = (end - start) // self.world
+        return start + self.rank * c, c
+
+    def _process_sharded(self, start: int, end: int):
+        from ._lib import check, lib, ptr
+        P = self.P
+        s0, c = self._shard(start, end)
+        op = dist.ReduceOp.AVG if self.use_avg else dist.ReduceOp.SUM
+        dist.reduce_scatter_tensor(P.grad[s0:s0 + c], P.grad[start:end], op=op, group=self.group)
+        if not self.use_avg:
+            P.grad[s0:s0 + c].div_(self.world)
+        self.optimizer.step_range(s0, s0 + c)
+        dist.all_gather_into_tensor(P.master[start:end], P.master[s0:s0 + c], group=self.group)
+        check(lib.nl_cast_bf16(ptr(P.master[start:]), ptr(P.shadow[start:]), end - start,
+                               torch.cuda.current_stream().cuda_stream), "nl_cast_bf16")
+
+    def gather_sharded(self, bufs):
+        """Sharded mode: make every rank's copy of ``bufs`` (flat buffers such
+        as the reduced gradient or the AdamW moments, each valid only on the
+        rank's own shard of each bucket) whole again.  Collective: every rank
+        calls it."""
+        if not self.sharded:
+            return
+        torch.cuda.current_stream().wait_stream(self.stream)
+        for start, end, names in self.buckets:
+            if self.sparse and names == {"wte"}:
+                continue
+            s0, c = self._shard(start, end)
+            for b in bufs:
+                dist.all_gather_into_tensor(b[start:end], b[s0:s0 + c].clone(), group=self.group)
 
     def _process_rows(self):
         """The token table after the backward: touched rows only."""
@@ -261,6 +307,7 @@ class TrainConfig:
     keep_grads: bool = True
     sparse_embedding_rows: bool = True  # token-table AdamW by rows: untouched rows at the step's start
     compact_embedding_exchange: bool = False  # and all-reduce only the touched rows (host waits for their count)
+    sharded_optimizer: bool = False   # N > 1: reduce-scatter + AdamW on this rank's shard + all-gather
 
 
 class Trainer:
@@ -280,7 +327,8 @@ class Trainer:
         overlap = self.device.type == "cuda" or world > 1
         self.reducer = BucketReducer(self.P, tcfg.bucket_mb << 20, group, optimizer=self.opt if overlap else None,
                                      sparse_rows=tcfg.sparse_embedding_rows and self.device.type == "cuda",
-                                     compact_exchange=tcfg.compact_embedding_exchange)
+                                     compact_exchange=tcfg.compact_embedding_exchange,
+                                     sharded=tcfg.sharded_optimizer)
         self.loader = ZipfLoader(tcfg.batch, tcfg.seq, cfg.vocab, tcfg.seed, rank)
         self.step_idx = 0
         self.warmup = min(tcfg.warmup, tcfg.steps // 5)
@@ -405,7 +453,16 @@ class Trainer:
         return float(self._loss_slots[k][0])
 
     # ------------------------------------------------------------- checkpoint
+    def gather_state(self, grads: bool = False):
+        """With the sharded optimizer each rank holds its own shard of the AdamW
+        moments (and of the reduced gradient): all-gather them so that every
+        rank has the whole state.  Collective (every rank calls it); a no-op
+        otherwise.  save / save_reference call it."""
+        bufs = [self.P.exp_avg, self.P.exp_avg_sq] + ([self.P.grad] if grads else [])
+        self.reducer.gather_sharded(bufs)
+
     def save(self, path: str):
+        self.gather_state()
         if self.rank != 0:
             return
         state = {"params": self.P.state_dict(), "step": self.step_idx, "opt_t": self.opt.t,
@@ -427,6 +484,7 @@ class Trainer:
         """Resume state in the reference's pickle format ({params, opt_state,
         step}, nested numpy trees; nlearn/train.py:74-87)."""
         from .checkpoint import save_resume_state
+        self.gather_state()
         if self.rank != 0:
             return
         save_resume_state(self._named(self.P.master), self._named(self.P.exp_avg), self._named(self.P.exp_avg_sq),

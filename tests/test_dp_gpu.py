@@ -7,7 +7,8 @@ same kernels, but bf16 activation gradients are rounded from f32 sums whose
 order varies run to run (TMA reduce-adds), so the 1-GPU step is itself
 reproducible only to a noise floor: the test measures that floor by running
 the 1-GPU step twice, and requires, per tensor, the data-parallel gradient to
-sit within 4x that floor or 1e-3 of the 1-GPU one, both as max |err| /
+sit within 4x that floor or 1e-3 of the 1-GPU one, in all three exchange modes (whole token-table all-reduce,
+touched rows only, sharded optimizer), both as max |err| /
 max |ref| and normwise, and every element larger than a tenth of its
 tensor's largest within 1e-2 relative, or 4x the worst such relative
 difference between the two 1-GPU runs.  The replicas' weights must stay
@@ -37,12 +38,15 @@ def _rank(rank, world, port, out):
     from nlearn_b200.model import GPTConfig
     from nlearn_b200.train import Trainer, TrainConfig
     res = {}
-    for compact in (False, True):   # whole token-table all-reduce, and touched rows only
+    # whole token-table all-reduce; touched rows only; sharded optimizer
+    for mode in ("dense", "compact", "sharded"):
         tr = Trainer(GPTConfig(), TrainConfig(batch=2, seq=128, steps=10, warmup=0, bucket_mb=16, keep_grads=True,
-                                              compact_embedding_exchange=compact), f"cuda:{rank}", rank, world)
+                                              compact_embedding_exchange=mode == "compact",
+                                              sharded_optimizer=mode == "sharded"), f"cuda:{rank}", rank, world)
         losses = [tr.train_step(*tr.loader.next()) for _ in range(STEPS)]
+        tr.gather_state(grads=True)   # (sharded: each rank's reduced-gradient shard -> whole buffer)
         torch.cuda.synchronize()
-        res[compact] = (tr.P.master.cpu().numpy(), losses, tr.P.grad.cpu().numpy())
+        res[mode] = (tr.P.master.cpu().numpy(), losses, tr.P.grad.cpu().numpy())
         del tr
     out[rank] = res
     dist.destroy_process_group()
@@ -57,9 +61,9 @@ def test_dp2_matches_single_gpu_full_batch():
     out = mgr.dict()
     mp.spawn(_rank, args=(2, 29600 + os.getpid() % 300, out), nprocs=2, join=True)
     modes = []
-    for compact in (False, True):
-        m0, l0, g0 = out[0][compact]
-        m1, _, g1 = out[1][compact]
+    for mode in ("dense", "compact", "sharded"):
+        m0, l0, g0 = out[0][mode]
+        m1, _, g1 = out[1][mode]
         assert np.array_equal(m0, m1)  # replicas stay identical
         assert np.array_equal(g0, g1)  # both hold the same reduced gradient
         modes.append((m0, g0))
