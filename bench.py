@@ -511,8 +511,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sharded-optimizer", action="store_true",
                     help="N > 1: reduce-scatter, AdamW on this rank's shard, all-gather the weights")
-    ap.add_argument("--compact-exchange", action="store_true",
-                    help="all-reduce only the token-table rows the batch touched (N > 1)")
+    ap.add_argument("--dense-exchange", action="store_true",
+                    help="all-reduce the whole token-table gradient instead of the touched rows (N > 1)")
     ap.add_argument("--no-long", action="store_true", help="skip the seq-4096 long-context measurement")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of CUDA-graph replay")
     ap.add_argument("--no-extras", action="store_true",
@@ -534,7 +534,7 @@ def main():
     torch.cuda.set_device(dev)
     cfg = GPTConfig()
     tr = Trainer(cfg, TrainConfig(batch=BATCH, seq=SEQ, steps=1000, peak_lr=1e-3, warmup=200,
-                                  compact_embedding_exchange=args.compact_exchange,
+                                  compact_embedding_exchange=not args.dense_exchange,
                                   sharded_optimizer=args.sharded_optimizer), dev, rank, world)
 
     # device-resident batches for the timed region

@@ -306,8 +306,13 @@ class TrainConfig:
     # land on the side stream while the backward runs), so off by default
     keep_grads: bool = True
     sparse_embedding_rows: bool = True  # token-table AdamW by rows: untouched rows at the step's start
-    compact_embedding_exchange: bool = False  # and all-reduce only the touched rows (host waits for their count)
-    sharded_optimizer: bool = False   # N > 1: reduce-scatter + AdamW on this rank's shard + all-gather
+    # and all-reduce only the touched rows (the host waits, after the backward,
+    # for their count, known since the step's start); measured at 2 ranks:
+    # tail 0.37 -> 0.22 ms, 6.27 -> 6.19 ms/step
+    compact_embedding_exchange: bool = True
+    # N > 1: reduce-scatter + AdamW on this rank's shard + all-gather; measured
+    # at 2 ranks no faster than the all-reduce (6.34 vs 6.27 ms/step), so off
+    sharded_optimizer: bool = False
 
 
 class Trainer:
